@@ -1,0 +1,429 @@
+"""Benchmark of the b200 sparse hot path (one JSON line on rank 0).
+
+Workload (the configuration the 1/2/4/8-GPU metric is quoted
+on, which fits one B200): C4 -- an 8,000,000 x 8,000,000 CSR matrix with 32 distinct
+uniformly drawn columns per row (256M nonzeros, int64 indices, fp64 values U(-1,1)),
+row-sharded nnz-balanced over the N GPUs, and 20 power iterations x <- A x / ||A x||
+from a seeded U(-1,1) x0.  One STEP is one such 20-iteration solve (set x0, 20 fused
+SpMV+norm kernels with the shard exchange between them, finalise).  Strong scaling:
+the matrix is the same at every N.
+
+Metric: effective HBM GB/s = compulsory SpMV bytes (8(M+1) + 16 nnz + 8 N + 8 M for the
+whole matrix) x 20 iterations / step time, whole job, max over ranks.  `value` has A and
+x0 resident in HBM; `e2e` repeats the step through the public API from pinned host
+buffers (H2D of the shard, column renumbering, 20 iterations, D2H of x and lambda).
+The inputs (4.29 GB) exceed the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+C4_N = 8_000_000
+C4_PER_ROW = 32
+C4_SEED = 4
+X0_SEED = 7
+ITERS = 20
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--rows", type=int, default=C4_N, help="matrix size (default: the C4 config)")
+    ap.add_argument("--iters", type=int, default=ITERS)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--tpr", type=int, default=8)
+    ap.add_argument("--unroll", type=int, default=2)
+    ap.add_argument("--vec", type=int, default=2)
+    ap.add_argument("--block", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def spmv_bytes(rows: int, cols: int, nnz: int) -> int:
+    """Compulsory bytes of one CSR SpMV: indptr + indices + values + x + y."""
+    return 8 * (rows + 1) + 16 * nnz + 8 * cols + 8 * rows
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_record(workload: str, kernel: str):
+    """dram bytes per launch from the committed ncu summary (profiles/traffic.json)."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as fh:
+        d = json.load(fh)
+    rec = d.get(workload, {}).get(kernel)
+    return rec
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_reference_spmv(A, x_len: int):
+    """The reference's own OpenMP SpMV (oracle/_ref, rebuilt with -march=native when a
+    compiler exists) or, failing that, the oracle's OpenMP port.  Returns
+    (callable(x, y), kind, description, threads)."""
+    from oracle import build as ob
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    libs = None
+    native_dir = os.path.join("/tmp", "tilegen_ref_native")
+    if os.path.exists(ob.GEN_DIR):
+        libs = ob.rebuild_ref_native(native_dir)
+        march = "native"
+        if not libs:
+            libs = O.ref_omp_libs()
+            march = "x86-64-v3"
+    if libs:
+        M, N, nnz = A.rows, A.cols, A.nnz
+        ip, ix, d = A.indptr, A.indices, A.data
+        best = None
+        for cfg in ("T32U1", "T64U2", "T128U4"):  # small CPU autotune, budget 3
+            stem = "ref_omp_spmv_f64_%s" % cfg
+            if stem not in libs:
+                continue
+            k = O.RefOmpKernel(libs[stem], "spmv")
+            y = np.empty(M)
+            xx = np.ones(N)
+            k(ip, ix, d, xx, y, M, N, nnz)
+            t0 = time.perf_counter()
+            k(ip, ix, d, xx, y, M, N, nnz)
+            dt = time.perf_counter() - t0
+            if best is None or dt < best[0]:
+                best = (dt, cfg, k)
+        if best is not None:
+            k = best[2]
+            return ((lambda x, y: k(ip, ix, d, x, y, M, N, nnz)), "reference",
+                    "reference OpenMP launch_spmv (tilegen codegen cpu backend, %s, -O3 -march=%s -fopenmp)"
+                    % (best[1], march), threads)
+    return ((lambda x, y: O.spmv_omp(A, x, out=y)), "port", "oracle OpenMP port of cpp/src/ref.cpp:6-15", threads)
+
+
+def cpu_power_sample(A, x0, iters: int, spmv):
+    """`iters` power iterations on the host; returns seconds."""
+    x = x0.copy()
+    y = np.empty(A.rows)
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        spmv(x, y)
+        nrm = float(np.sqrt(np.dot(y, y)))
+        np.multiply(y, 1.0 / nrm, out=x)
+    return time.perf_counter() - t0
+
+
+def run_reference(args, rank: int, world: int):
+    """--impl reference: the reference's CPU implementation of the path, rank 0 only."""
+    if rank != 0:
+        return 0
+    from tilegen_b200 import matrices as Mx
+
+    n = args.rows
+    A = Mx.c4_rows(0, n, n=n, per_row=C4_PER_ROW, seed=C4_SEED)
+    x0 = np.random.default_rng([X0_SEED, 0]).uniform(-1.0, 1.0, size=n)
+    spmv, kind, desc, threads = cpu_reference_spmv(A, n)
+    iters_per_step = 2
+    for _ in range(args.warmup):
+        cpu_power_sample(A, x0, 1, spmv)
+    times = [cpu_power_sample(A, x0, iters_per_step, spmv) for _ in range(args.steps)]
+    bytes_iter = spmv_bytes(n, n, A.nnz)
+    sec = float(np.mean(times))
+    gbs = bytes_iter * iters_per_step / sec / 1e9
+    sample = "%d of the %d power iterations per step on the full %dx%d matrix (%d nnz)" % (
+        iters_per_step, ITERS, n, n, A.nnz)
+    line = {
+        "impl": "reference",
+        "metric": "effective_hbm_gbs_power_iteration_spmv",
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f64",
+        "data": "synthetic (seeded C4 generator)",
+        "config": workload_config(n, world),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": sample, "impl": desc},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(n: int, world: int):
+    return {"workload": "C4 power iteration: %dx%d CSR, %d distinct cols/row, fp64, %d iterations/step"
+                        % (n, n, C4_PER_ROW, ITERS),
+            "rows": n, "nnz": n * C4_PER_ROW, "iterations_per_step": ITERS,
+            "parallelism": "row-sharded x%d, x replicated (in-place NCCL all-gather of shards)" % world,
+            "l2": "inputs (%.2f GB) larger than L2 (126 MB): no flush" % (spmv_bytes(n, n, n * C4_PER_ROW) / 1e9)}
+
+
+# ----------------------------------------------------------------------------- b200 arm
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    from tilegen_b200 import lib, matrices as Mx
+    from tilegen_b200.power import PowerIteration, uniform_bounds
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    n = args.rows
+    bounds = uniform_bounds(n, world)
+    r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
+    shard = Mx.c4_rows(r0, r1, n=n, per_row=C4_PER_ROW, seed=C4_SEED)
+    x0_all = np.random.default_rng([X0_SEED, 0]).uniform(-1.0, 1.0, size=n)
+    x0 = x0_all[r0:r1].copy()
+
+    # pinned host copies (the e2e inputs)
+    h_ip = torch.from_numpy(shard.indptr).pin_memory()
+    h_ix = torch.from_numpy(shard.indices).pin_memory()
+    h_d = torch.from_numpy(shard.data).pin_memory()
+    h_x0 = torch.from_numpy(x0).pin_memory()
+    h_xout = torch.empty(r1 - r0, dtype=torch.float64).pin_memory()
+    h_lam = torch.empty(1, dtype=torch.float64).pin_memory()
+
+    s = lib.default_schedule()
+    s.threads_per_row, s.unroll, s.vector_width, s.block_size, s.tile = args.tpr, args.unroll, args.vec, args.block, 32
+    lib.validate_schedule(s)
+
+    d_ip = h_ip.to(dev)
+    d_ix = h_ix.to(dev)
+    d_d = h_d.to(dev)
+    d_x0 = h_x0.to(dev)
+    pi = PowerIteration(d_ip, d_ix, d_d, bounds, rank, sched=s)
+    del d_ix
+    x_out = torch.empty(r1 - r0, dtype=torch.float64, device=dev)
+    lam = torch.empty(1, dtype=torch.float64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    kernel_events = []
+
+    def one_step(record_kernels: bool):
+        pi.set_x0(d_x0)
+        if record_kernels:
+            evs = []
+
+            def on_step(i):
+                e = torch.cuda.Event(enable_timing=True)
+                e.record(stream)
+                evs.append(e)
+
+            pi.iterate(args.iters, on_step)
+            kernel_events.append(evs)
+        else:
+            pi.iterate(args.iters)
+        pi.result(x_out, lam)
+
+    for _ in range(args.warmup):
+        one_step(False)
+    barrier()
+
+    launches0 = pi.kernel_launches
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    wall0 = time.perf_counter()
+    t_start.record(stream)
+    for _ in range(args.steps):
+        one_step(True)
+    t_end.record(stream)
+    barrier()
+    wall = time.perf_counter() - wall0
+    clocks = sampler.stop() if sampler else None
+    launches = pi.kernel_launches - launches0
+    ms_local = t_start.elapsed_time(t_end)
+    kdur = [evs[2 * k].elapsed_time(evs[2 * k + 1]) for evs in kernel_events for k in range(args.iters)]
+    k_ms_local = float(np.mean(kdur))
+
+    # ---- e2e through the public API from pinned host buffers
+    e2e_ms = []
+    for it in range(args.e2e_steps + 1):
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ip = h_ip.to(dev, non_blocking=True)
+        ix = h_ix.to(dev, non_blocking=True)
+        dd = h_d.to(dev, non_blocking=True)
+        xx = h_x0.to(dev, non_blocking=True)
+        pe = PowerIteration(ip, ix, dd, bounds, rank, sched=s)
+        del ix
+        pe.set_x0(xx)
+        pe.iterate(args.iters)
+        xo, lo = pe.result()
+        h_xout.copy_(xo, non_blocking=True)
+        h_lam.copy_(lo, non_blocking=True)
+        e1.record(stream)
+        barrier()
+        if it > 0:  # the first pass warms allocator and communicator buffers
+            e2e_ms.append(e0.elapsed_time(e1))
+        del pe, ip, dd, xx
+    e2e_local = float(np.mean(e2e_ms))
+
+    # ---- max over ranks
+    vals = torch.tensor([ms_local, k_ms_local, e2e_local], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_total, k_ms, e2e_step_ms = [float(v) for v in vals.cpu()]
+    ms_step = ms_total / args.steps
+    total_bytes = spmv_bytes(n, n, n * C4_PER_ROW)
+    gbs = total_bytes * args.iters / (ms_step / 1e3) / 1e9
+    e2e_gbs = total_bytes * args.iters / (e2e_step_ms / 1e3) / 1e9
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        local_bytes = spmv_bytes(r1 - r0, n, shard.nnz)
+        achieved = local_bytes / (k_ms / 1e3) / 1e9
+        tr = traffic_record("c4_%d" % world, "power_step_kernel")
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"
+                    if peak_kind == "measured" else "fallback 6.65 TB/s",
+                    "kernel": "power_step_kernel", "kernel_ms": round(k_ms, 4),
+                    "algorithmic_bytes_per_launch": local_bytes,
+                    "traffic": tr["dram_bytes_per_launch"] if tr else None}
+        line = {
+            "metric": "effective_hbm_gbs_power_iteration_spmv",
+            "value": round(gbs, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f64",
+            "data": "synthetic (seeded C4 generator, values U(-1,1))",
+            "config": workload_config(n, world),
+            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(h_ip.numel() * 8 + h_ix.numel() * 8 + h_d.numel() * 8 + h_x0.numel() * 8),
+                    "d2h_bytes_per_step": int(h_xout.numel() * 8 + 8), "ms_per_step": round(e2e_step_ms, 3)},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "clocks": clocks,
+            "wall_s_timed": round(wall, 4),
+            "schedule": {"tpr": args.tpr, "unroll": args.unroll, "vec": args.vec, "block": args.block},
+            "lambda": float(h_lam[0]),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(shard, x0_all)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def cpu_baseline(A, x0):
+    spmv, kind, desc, threads = cpu_reference_spmv(A, A.cols)
+    iters = 3
+    cpu_power_sample(A, x0, 1, spmv)
+    sec = cpu_power_sample(A, x0, iters, spmv)
+    gbs = spmv_bytes(A.rows, A.cols, A.nnz) * iters / sec / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": "%d of the %d power iterations on the full matrix (%d rows, %d nnz), host cores"
+                      % (iters, ITERS, A.rows, A.nnz), "impl": desc}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,191 @@
+/*
+ * tilegen_b200.h -- C ABI of libtilegen_b200.so, the sm_100a (B200) sparse hot path.
+ *
+ * Two layers are exported:
+ *
+ *  1. Reference-compatible launchers.  `launch_spmv`, `launch_spmm`, `launch_sddmm`,
+ *     `launch_fused_spmv_axpy` and `launch_axpy` have exactly the signatures that
+ *     TileGen's code generator emits (tilegen/codegen.py:226-280, ctypes argtypes in
+ *     tilegen/verify.py:166-173).  Like the reference they take DEVICE pointers owned
+ *     by the caller (tilegen/verify.py:414-420), run on the legacy default stream and
+ *     end with a device-wide synchronize (tilegen/codegen.py:798), so
+ *     `tilegen.verify.run_kernel` and `tilegen.autotune._make_caller` can drive them
+ *     unchanged.  They read the schedule set by `tg_set_schedule` (process-global).
+ *     Differences from the reference, all in the safe direction: SpMM writes C
+ *     instead of accumulating into it (a caller that pre-zeroes C, as
+ *     tilegen/verify.py:437 does, sees the same result), and the status of the last
+ *     call is kept for `tg_last_status` / `tg_last_error_string`.
+ *
+ *  2. The native API (`tg_*`).  Asynchronous on the given CUDA stream, no internal
+ *     synchronisation, no allocation: the caller passes a workspace of
+ *     `tg_*_workspace_bytes(...)` bytes (NULL/0 when that size is 0).  Every call
+ *     returns TG_OK (0) or a negative TG_E* status; the message is available from
+ *     `tg_last_error_string()` on the calling host thread.  Calls on distinct
+ *     streams/devices from distinct host threads are safe.
+ *
+ * Layout of the sparse operand (identical to the reference, tilegen/verify.py:318-335):
+ * CSR with int64 `indptr[rows+1]` (non-decreasing, indptr[0] == 0, indptr[rows] == nnz),
+ * int64 `indices[nnz]` in [0, cols) and values `data[nnz]`.  Dense operands are
+ * row-major and contiguous.  All pointers are device pointers.
+ */
+#ifndef TILEGEN_B200_H
+#define TILEGEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TG_API __attribute__((visibility("default")))
+#else
+#define TG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define TG_OK 0
+#define TG_EINVAL -1       /* bad argument (null pointer, negative size, bad schedule) */
+#define TG_ECUDA -2        /* a CUDA runtime call or kernel launch failed */
+#define TG_ENOMEM -3       /* workspace too small, or the library's own allocation failed */
+#define TG_EUNSUPPORTED -4 /* no kernel instance for this schedule / device */
+#define TG_ETIMEDOUT -5    /* a bounded device-side wait ran out (multi-GPU paths) */
+#define TG_EBOUNDS -6      /* bounds checking found an index out of range */
+
+/* CUDA stream handle (a cudaStream_t); NULL is the legacy default stream. */
+typedef void* tg_stream_t;
+
+/* ------------------------------------------------------------------ schedule */
+/* Row-to-thread mapping of the kernels. */
+#define TG_SPLIT_ROWWISE 0 /* reference mapping: T rows per CTA tile, TPR lanes per row */
+#define TG_SPLIT_MERGE 1   /* nnz-balanced chunks, rows split across chunks + fix-up */
+#define TG_SPLIT_AUTO 2    /* library picks from the row-length statistics */
+
+/* flags */
+#define TG_FLAG_BOUNDS_CHECK 1u /* validate indptr/indices on the device; TG_EBOUNDS on error */
+#define TG_FLAG_INJECT_BUG 2u   /* deliberately skip the last row (harness self-test) */
+
+/*
+ * Mirrors tilegen.codegen.Lowering (tilegen/codegen.py:90-134): each knob of the
+ * reference's Config/schedule IR is one field here and one template parameter of
+ * the kernels.  Zero in any field selects the library default for that knob.
+ */
+typedef struct tg_sched {
+    int32_t tile;            /* T: rows per CTA tile (Tile, passes.py:243-270)            */
+    int32_t threads_per_row; /* TPR: lanes cooperating on one row (ThreadsPerRow)        */
+    int32_t unroll;          /* U: independent loads in flight per lane (Unroll)          */
+    int32_t vector_width;    /* V: elements per vector load (Vectorize)                   */
+    int32_t block_size;      /* B: threads per CTA (Parallelize block_size)               */
+    int32_t split;           /* TG_SPLIT_*                                                */
+    int32_t chunk_nnz;       /* merge split: nonzeros per chunk (0 = library default)     */
+    uint32_t flags;          /* TG_FLAG_*                                                 */
+} tg_sched;
+
+/* CSR operand; `data` is double* for *_f64 entry points and float* for *_f32. */
+typedef struct tg_csr {
+    int64_t rows;
+    int64_t cols;
+    int64_t nnz;
+    const int64_t* indptr;
+    const int64_t* indices;
+    const void* data;
+} tg_csr;
+
+/* ------------------------------------------------------------ library / errors */
+TG_API const char* tg_version(void);
+/* Message for the last failing tg_* / launch_* call on this host thread ("" if none). */
+TG_API const char* tg_last_error_string(void);
+/* Status of the last reference-compatible launch_* call on this host thread. */
+TG_API int tg_last_status(void);
+/* Fills *s with the library defaults (reference BASELINE T32/TPR1/U1/V1/B128,
+ * tilegen/autotune.py:55-56, with split = TG_SPLIT_ROWWISE). */
+TG_API void tg_default_schedule(tg_sched* s);
+/* Checks a schedule; returns TG_OK or TG_EINVAL (reason in tg_last_error_string). */
+TG_API int tg_validate_schedule(const tg_sched* s);
+
+/* Process-global schedule read by the launch_* shims (not by the tg_* API). */
+TG_API int tg_set_schedule(const tg_sched* s);
+TG_API int tg_get_schedule(tg_sched* s);
+
+/* ----------------------------------------------------------- workspace sizing */
+/* Bytes of device workspace needed by the tg_* call with the same arguments.
+ * `k` is the dense width (K) for SpMM/SDDMM and 1 for SpMV. */
+TG_API size_t tg_spmv_workspace_bytes(int64_t rows, int64_t nnz, const tg_sched* s);
+TG_API size_t tg_spmm_workspace_bytes(int64_t rows, int64_t nnz, int64_t k, const tg_sched* s);
+TG_API size_t tg_sddmm_workspace_bytes(int64_t rows, int64_t nnz, int64_t k, const tg_sched* s);
+
+/* ------------------------------------------------------------------ native API */
+/* y[i] = sum_p data[p] * x[indices[p]]          (ref: tilegen/codegen.py:592-643,
+ * math cpp/src/ref.cpp:6-15). fp64 in, fp64 accumulate. */
+TG_API int tg_spmv_f64(const tg_csr* A, const double* x, double* y, const tg_sched* s,
+                void* workspace, size_t workspace_bytes, tg_stream_t stream);
+/* fp32 values/x/y with fp32 accumulation (north_star: rel. error <= 1e-4). */
+TG_API int tg_spmv_f32(const tg_csr* A, const float* x, float* y, const tg_sched* s,
+                void* workspace, size_t workspace_bytes, tg_stream_t stream);
+/* z[i] = alpha * (A x)[i] + beta * w[i]       (ref: tilegen/dsl.py:237-247 after
+ * loop_fusion, tilegen/passes.py:188-240; math cpp/src/ref.cpp:62-73). */
+TG_API int tg_fused_spmv_axpy_f64(const tg_csr* A, const double* x, const double* w, double* z,
+                           double alpha, double beta, const tg_sched* s, void* workspace,
+                           size_t workspace_bytes, tg_stream_t stream);
+/* C[i,:] = sum_p data[p] * B[indices[p],:]; B is cols x k, C is rows x k, row-major.
+ * C is overwritten (ref: tilegen/codegen.py:646-685, math cpp/src/ref.cpp:31-43). */
+TG_API int tg_spmm_f32(const tg_csr* A, const float* B, float* C, int64_t k, const tg_sched* s,
+                void* workspace, size_t workspace_bytes, tg_stream_t stream);
+TG_API int tg_spmm_f64(const tg_csr* A, const double* B, double* C, int64_t k, const tg_sched* s,
+                void* workspace, size_t workspace_bytes, tg_stream_t stream);
+/* out[p] = data[p] * dot(U[i,:], V[indices[p],:]) for p in row i; U is rows x k,
+ * V is cols x k.  The output pattern is A's (indptr/indices unchanged)
+ * (ref: tilegen/codegen.py:688-714, math cpp/src/ref.cpp:46-59). */
+TG_API int tg_sddmm_f32(const tg_csr* A, const float* U, const float* V, float* out, int64_t k,
+                 const tg_sched* s, void* workspace, size_t workspace_bytes,
+                 tg_stream_t stream);
+TG_API int tg_sddmm_f64(const tg_csr* A, const double* U, const double* V, double* out, int64_t k,
+                 const tg_sched* s, void* workspace, size_t workspace_bytes,
+                 tg_stream_t stream);
+/* z = alpha * x + beta * w (ref: tilegen/dsl.py:250-256, tilegen/codegen.py:580-589). */
+TG_API int tg_axpy_f64(const double* x, const double* w, double* z, double alpha, double beta,
+                int64_t n, const tg_sched* s, tg_stream_t stream);
+
+/* ------------------------------------------------------ power iteration (new) */
+/* Iterated SpMV x <- A x / ||A x||, one process per GPU, rows split into `nparts`
+ * contiguous shards.  No counterpart in the reference (north_star's multi-GPU mode).
+ * The iterate is a padded vector of nparts * stride doubles: shard r occupies
+ * [r*stride, r*stride + rows_r) and its last element r*stride + stride - 1 (the slot)
+ * holds sum(shard^2).  A's column indices must be renumbered to this layout
+ * (j -> owner(j) * stride + j - first_row(owner)).  The workspace must be zero-filled
+ * before its first use; every call leaves it zeroed. */
+TG_API size_t tg_power_workspace_bytes(void);
+/* y[0..rows) = A x / sqrt(sum of the nparts slots of x); y[stride-1] = sum(y^2). */
+TG_API int tg_power_step_f64(const tg_csr* A, const double* x, int32_t nparts, int64_t stride,
+                             double* y, const tg_sched* s, void* workspace,
+                             size_t workspace_bytes, tg_stream_t stream);
+/* shard[stride-1] = sum(shard[0..rows)^2) (slot of an initial iterate). */
+TG_API int tg_shard_norm2_f64(double* shard, int64_t rows, int64_t stride, void* workspace,
+                              size_t workspace_bytes, tg_stream_t stream);
+/* x_out[0..rows) = shard `part` of x divided by sqrt(sum of slots); *lambda = that norm. */
+TG_API int tg_power_finalize_f64(const double* x, int32_t nparts, int64_t stride, int32_t part,
+                                 int64_t rows, double* x_out, double* lambda_out,
+                                 tg_stream_t stream);
+
+/* --------------------------------------------- reference-compatible launchers */
+/* Signatures as emitted by tilegen/codegen.py:_abi (226-280) for the standard kernels
+ * of tilegen/dsl.py:214-256; argument order/meaning as in tilegen/verify.py:166-173. */
+TG_API void launch_spmv(const int64_t* indptr, const int64_t* indices, const double* data,
+                 const double* x, double* y, int64_t M, int64_t N, int64_t nnz);
+TG_API void launch_spmm(const int64_t* indptr, const int64_t* indices, const double* data,
+                 const double* B, double* C, int64_t M, int64_t N, int64_t K, int64_t nnz);
+TG_API void launch_sddmm(const int64_t* indptr, const int64_t* indices, const double* data,
+                  const double* U, const double* V, double* C, int64_t M, int64_t N,
+                  int64_t K, int64_t nnz);
+TG_API void launch_fused_spmv_axpy(const int64_t* indptr, const int64_t* indices,
+                            const double* data, const double* x, const double* w, double* z,
+                            double alpha, double beta, int64_t M, int64_t N, int64_t nnz);
+TG_API void launch_axpy(const double* x, const double* w, double* z, double alpha, double beta,
+                 int64_t M);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILEGEN_B200_H */

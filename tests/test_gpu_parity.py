@@ -1,0 +1,283 @@
+"""GPU parity of the b200 kernels against the reference's outputs and the CPU oracle.
+
+Shaped like the reference's CUDA suite (tests/test_cuda_gpu.py:32-104): every standard
+kernel x the same seven schedules on the 257x257 edge matrix, compared with the
+reference's SciPy float64 outputs under the reference tolerance
+(8 * eps * max_row_nnz * max|ref| + 1e-12, tilegen/verify.py:510-514) and, per
+north_star, a relative error <= 1e-9 for fp64 / <= 1e-4 for fp32 accumulation with the
+relative error defined as |d| / max(|ref|, 1e-3 * max|ref|).  Then the merge split, the
+reference-ABI launchers, corpus and BASELINE matrices at full size, and edge cases.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tilegen_b200 import codegen as cg
+from tilegen_b200 import device as D
+from tilegen_b200 import lib
+from tilegen_b200 import matrices as M
+from tilegen_b200.verify import inputs_for, run_kernel, run_launcher, tolerance, verify
+
+from conftest import edge_data
+
+pytestmark = pytest.mark.gpu
+
+KERNELS = ["spmv", "spmm", "sddmm", "fused_spmv_axpy", "axpy"]
+
+# tests/test_cuda_gpu.py:36-44
+REF_SCHEDULES = [
+    cg.Config(tile_size=32, threads_per_row=1, unroll=1, vector_width=1, block_size=128),
+    cg.Config(tile_size=32, threads_per_row=2, unroll=2, vector_width=1, block_size=128),
+    cg.Config(tile_size=64, threads_per_row=4, unroll=4, vector_width=2, block_size=256),
+    cg.Config(tile_size=128, threads_per_row=8, unroll=2, vector_width=2, block_size=512),
+    cg.Config(tile_size=32, threads_per_row=32, unroll=8, vector_width=2, block_size=512),
+    cg.Config(tile_size=1, threads_per_row=4, unroll=1, vector_width=1, block_size=128),
+    cg.Config(tile_size=256, threads_per_row=1, unroll=4, vector_width=1, block_size=256),
+]
+B200_SCHEDULES = [
+    cg.Config(split="merge", block_size=256),
+    cg.Config(split="merge", block_size=128, threads_per_row=8, unroll=4, vector_width=4, chunk_nnz=64),
+    cg.Config(split="merge", block_size=512, threads_per_row=32, unroll=2, vector_width=2, chunk_nnz=16),
+    cg.Config(tile_size=64, threads_per_row=16, unroll=4, vector_width=4, block_size=256),
+]
+ALL = REF_SCHEDULES + B200_SCHEDULES
+IDS = ["%s-T%d-TPR%d-U%d-V%d-B%d" % (c.split, c.tile_size, c.threads_per_row, c.unroll, c.vector_width, c.block_size)
+       for c in ALL]
+
+
+def rel_err(out, ref):
+    out, ref = np.asarray(out, np.float64).ravel(), np.asarray(ref, np.float64).ravel()
+    if ref.size == 0:
+        return 0.0
+    floor = 1e-3 * max(np.abs(ref).max(), 1e-300)
+    return float((np.abs(out - ref) / np.maximum(np.abs(ref), floor)).max())
+
+
+def check_f64(out, ref, A):
+    out, ref = np.asarray(out).ravel(), np.asarray(ref).ravel()
+    tol = tolerance(A, ref)
+    d = float(np.abs(out - ref).max()) if ref.size else 0.0
+    assert d <= tol, "max abs err %.3g > tol %.3g" % (d, tol)
+    assert rel_err(out, ref) <= 1e-9
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    lib.load()
+    yield
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("cfg", ALL, ids=IDS)
+def test_kernel_matches_float64_reference(kernel, cfg, edge, edge_csr):
+    out = run_kernel(cg.generate(kernel, cfg), edge_csr, edge_data(edge), K=8)
+    check_f64(out, edge["ref_" + kernel], edge_csr)
+
+
+@pytest.mark.parametrize("kernel", ["spmv", "spmm", "sddmm"])
+@pytest.mark.parametrize("cfg", [REF_SCHEDULES[0], REF_SCHEDULES[3], B200_SCHEDULES[0], B200_SCHEDULES[1]],
+                         ids=["T32", "T128-TPR8", "merge256", "merge128"])
+def test_fp32_accumulation_within_1e_4(kernel, cfg, edge, edge_csr):
+    c = cg.Config(**{**cfg.to_dict(), "dtype": "f32"})
+    out = run_kernel(cg.generate(kernel, c), edge_csr, edge_data(edge), K=8)
+    assert rel_err(out, edge["ref_" + kernel]) <= 1e-4
+    # and against the reference's own fp32 OpenMP backend
+    assert rel_err(out, edge["omp_%s_f32" % kernel]) <= 1e-4
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("split", ["rowwise", "merge"])
+def test_injected_bug_is_caught(kernel, split, edge_csr):
+    cfg = cg.Config(tile_size=32, threads_per_row=4, unroll=2, vector_width=1, block_size=256, inject_bug=True,
+                    split=split)
+    res = verify(kernel, cfg, edge_csr, K=8)
+    assert not res.ok and res.max_abs_err > res.tolerance, res
+    good = verify(kernel, cg.Config(**{**cfg.to_dict(), "inject_bug": False}), edge_csr, K=8)
+    assert good.ok, good
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("cfg", [REF_SCHEDULES[0], REF_SCHEDULES[4], B200_SCHEDULES[0]], ids=["T32", "TPR32", "merge"])
+def test_reference_abi_launchers(kernel, cfg, edge, edge_csr):
+    """launch_<name> with device pointers and the process-global schedule, exactly as
+    the reference's verify.run_kernel calls a generated CUDA object."""
+    sched = cg.generate(kernel, cfg).sched
+    out = run_launcher(kernel, edge_csr, edge_data(edge), K=8, sched=sched)
+    check_f64(out, edge["ref_" + kernel], edge_csr)
+    lib.set_schedule(lib.default_schedule())
+
+
+@pytest.mark.parametrize("split", ["rowwise", "merge"])
+def test_corner_cases(corner, split):
+    for name in ("bug4", "empty_row3", "zeros2", "small3"):
+        shape = tuple(int(s) for s in corner[name + "_shape"])
+        A = M.CSR(corner[name + "_indptr"], corner[name + "_indices"], corner[name + "_data"], shape, name)
+        data = tuple(corner[name + "_" + k] for k in ("x", "w", "B", "U", "V")) + (0.7, -1.3)
+        for kernel in KERNELS:
+            out = run_kernel(cg.generate(kernel, cg.Config(unroll=2, split=split)), A, data, K=8)
+            check_f64(out, corner[name + "_ref_" + kernel], A)
+        if name == "zeros2":
+            out = run_kernel(cg.generate("spmv", cg.Config(unroll=4, split=split)), A, data, K=8)
+            assert np.all(out == 0.0)  # exact zero (tests/test_verify.py:39-43)
+
+
+@pytest.mark.parametrize("split", ["rowwise", "merge"])
+def test_empty_and_degenerate_shapes(split):
+    dev = torch.device("cuda")
+    s = cg.generate("spmv", cg.Config(split=split)).sched
+    # nnz == 0: every row is zero; rows == 0: nothing to do
+    for rows, cols in ((5, 7), (0, 3), (1, 1)):
+        A = D.DeviceCSR(torch.zeros(rows + 1, dtype=torch.int64, device=dev), torch.zeros(0, dtype=torch.int64, device=dev),
+                        torch.zeros(0, dtype=torch.float64, device=dev), (rows, cols))
+        y = torch.full((rows,), 7.0, dtype=torch.float64, device=dev)
+        D.spmv(A, torch.ones(cols, dtype=torch.float64, device=dev), y, sched=s)
+        assert torch.all(y == 0)
+        C = torch.full((rows, 4), 3.0, dtype=torch.float64, device=dev)
+        D.spmm(A, torch.ones((cols, 4), dtype=torch.float64, device=dev), C, sched=s)
+        assert torch.all(C == 0)
+    # trailing and leading empty rows around a single nonzero
+    m = M.CSR(np.array([0, 0, 0, 1, 1, 1], np.int64), np.array([2], np.int64), np.array([5.0]), (5, 3))
+    x = np.array([1.0, 2.0, 3.0])
+    out = run_kernel(cg.generate("spmv", cg.Config(split=split)), m, (x, x, None, None, None, 1.0, 1.0))
+    assert np.array_equal(out, [0, 0, 15.0, 0, 0])
+
+
+@pytest.mark.parametrize("cls", M.corpus_classes())
+@pytest.mark.parametrize("cfg", [cg.Config(threads_per_row=8, unroll=2, vector_width=2, block_size=256),
+                                 cg.Config(split="merge", block_size=256)], ids=["TPR8", "merge"])
+def test_corpus_classes_spmv_full(cls, cfg):
+    m = M.make_matrix(cls)
+    x = inputs_for("spmv", m, 8, 7)[0]
+    out = run_kernel(cg.generate("spmv", cfg), m, (x, None, None, None, None, 1.0, 1.0))
+    check_f64(out, O.spmv(m, x), m)
+
+
+@pytest.mark.parametrize("name", ["c1", "c2", "c3"])
+@pytest.mark.parametrize("cfg", [cg.Config(tile_size=64, threads_per_row=16, unroll=2, vector_width=2, block_size=256),
+                                 cg.Config(split="merge", block_size=256)], ids=["TPR16", "merge"])
+def test_baseline_spmv_configs_full_size(name, cfg):
+    m = M.baseline_matrix(name)
+    x = np.random.default_rng(11).uniform(-1, 1, m.cols)
+    out = run_kernel(cg.generate("spmv", cfg), m, (x, None, None, None, None, 1.0, 1.0))
+    check_f64(out, O.spmv(m, x), m)
+
+
+def _long_row_matrix():
+    """Rows of 1..3 nonzeros around three long rows (60000, 7001 and 2049 nonzeros), so
+    rows span many merge chunks, start/end mid-chunk, and chunk boundaries fall on row
+    boundaries too."""
+    rng = np.random.default_rng(17)
+    n = 70000
+    lens = rng.integers(0, 4, n)
+    lens[5], lens[40000], lens[n - 1] = 60000, 7001, 2049
+    indptr = np.zeros(n + 1, np.int64)
+    np.cumsum(lens, out=indptr[1:])
+    idx = np.concatenate([np.sort(rng.choice(n, size=L, replace=False)) if L else np.zeros(0, np.int64)
+                          for L in lens]).astype(np.int64)
+    return M.CSR(indptr, idx, rng.uniform(-1, 1, idx.size), (n, n), "longrows")
+
+
+@pytest.mark.parametrize("cfg", [cg.Config(split="merge", block_size=128), cg.Config(split="merge", block_size=256),
+                                 cg.Config(split="merge", threads_per_row=32, unroll=4, vector_width=2, chunk_nnz=32),
+                                 cg.Config(threads_per_row=32, unroll=4, vector_width=2)],
+                         ids=["merge128", "merge256", "merge-c32", "rowwise"])
+def test_long_rows_spanning_chunks(cfg):
+    m = _long_row_matrix()
+    data = inputs_for("spmm", m, 16, 3)
+    x, w, B, U, V, a, b = data
+    for kernel, ref in (("spmv", O.spmv(m, x)), ("fused_spmv_axpy", O.fused_spmv_axpy(m, x, w, a, b)),
+                        ("spmm", O.spmm(m, B)), ("sddmm", O.sddmm(m, U, V))):
+        out = run_kernel(cg.generate(kernel, cfg), m, data, K=16)
+        check_f64(out, ref, m)
+
+
+def test_merge_results_are_deterministic():
+    m = _long_row_matrix()
+    data = inputs_for("spmm", m, 16, 3)
+    g = cg.generate("spmv", cg.Config(split="merge"))
+    a = run_kernel(g, m, data)
+    b = run_kernel(g, m, data)
+    assert np.array_equal(a, b)
+    g = cg.generate("spmm", cg.Config(split="merge", chunk_nnz=32))
+    assert np.array_equal(run_kernel(g, m, data, K=16), run_kernel(g, m, data, K=16))
+
+
+@pytest.mark.parametrize("K", [1, 3, 8, 64, 100, 128, 600])
+@pytest.mark.parametrize("split", ["rowwise", "merge"])
+def test_dense_widths(K, split):
+    m = M.baseline_matrix("c3", scale=0.02)
+    data = inputs_for("spmm", m, K, 5)
+    for dtype in ("f64", "f32"):
+        cfg = cg.Config(threads_per_row=32, unroll=2, vector_width=4, split=split, dtype=dtype)
+        for kernel, ref in (("spmm", O.spmm(m, data[2])), ("sddmm", O.sddmm(m, data[3], data[4]))):
+            out = run_kernel(cg.generate(kernel, cfg), m, data, K=K)
+            if dtype == "f64":
+                check_f64(out, ref, m)
+            else:
+                assert rel_err(out, ref) <= 1e-4, (kernel, K, split)
+
+
+def test_misaligned_operands_use_safe_paths():
+    """Views that start one element into their allocation break 16-byte alignment; the
+    library must switch to scalar loads (no TMA, V=1) and stay correct."""
+    m = M.baseline_matrix("c1", scale=0.01)
+    dev = torch.device("cuda")
+    ip = torch.as_tensor(m.indptr).to(dev)
+    ix = torch.cat([torch.zeros(1, dtype=torch.int64), torch.as_tensor(m.indices)]).to(dev)[1:]
+    dv = torch.cat([torch.zeros(1, dtype=torch.float64), torch.as_tensor(m.data)]).to(dev)[1:]
+    assert ix.data_ptr() % 16 == 8
+    A = D.DeviceCSR(ip, ix, dv, m.shape)
+    x = np.random.default_rng(2).uniform(-1, 1, m.cols)
+    ref = O.spmv(m, x)
+    for cfg in (cg.Config(threads_per_row=8, vector_width=4, unroll=2), cg.Config(split="merge")):
+        y = D.spmv(A, torch.as_tensor(x).to(dev), sched=cg.generate("spmv", cfg))
+        check_f64(y.cpu().numpy(), ref, m)
+
+
+def test_bounds_check_reports_bad_index_without_computing():
+    dev = torch.device("cuda")
+    ip = torch.tensor([0, 2, 3], dtype=torch.int64, device=dev)
+    ix = torch.tensor([0, 5, 1], dtype=torch.int64, device=dev)  # 5 >= cols
+    A = D.DeviceCSR(ip, ix, torch.ones(3, dtype=torch.float64, device=dev), (2, 3))
+    y = torch.full((2,), -1.0, dtype=torch.float64, device=dev)
+    with pytest.raises(lib.TgError) as ei:
+        D.spmv(A, torch.ones(3, dtype=torch.float64, device=dev), y,
+               sched=cg.generate("spmv", cg.Config(bounds_check=True)))
+    assert ei.value.status == lib.TG_EBOUNDS and "out of range" in str(ei.value)
+    assert torch.all(y == -1.0)
+    ix[1] = 2
+    D.spmv(A, torch.ones(3, dtype=torch.float64, device=dev), y, sched=cg.generate("spmv", cg.Config(bounds_check=True)))
+    assert torch.allclose(y, torch.tensor([2.0, 1.0], dtype=torch.float64, device=dev))
+
+
+def test_workspace_too_small_is_an_error():
+    m = M.baseline_matrix("c1", scale=0.01)
+    A = D.DeviceCSR.from_host(m, "cuda")
+    s = cg.generate("spmv", cg.Config(split="merge")).sched
+    L = lib.load()
+    x = torch.zeros(m.cols, dtype=torch.float64, device="cuda")
+    y = torch.zeros(m.rows, dtype=torch.float64, device="cuda")
+    st = L.tg_spmv_f64(ctypes.byref(A.desc()), x.data_ptr(), y.data_ptr(), ctypes.byref(s), None, 0, None)
+    assert st == lib.TG_ENOMEM and "workspace" in lib.last_error()
+
+
+@pytest.mark.parametrize("split", ["rowwise", "merge"])
+def test_c5_spmm_sddmm_scaled(split):
+    m = M.baseline_matrix("c5", scale=0.05).astype(np.float32)
+    rng = np.random.default_rng(8)
+    B = rng.uniform(-1, 1, (m.cols, 128)).astype(np.float32)
+    U = rng.uniform(-1, 1, (m.rows, 64)).astype(np.float32)
+    V = rng.uniform(-1, 1, (m.cols, 64)).astype(np.float32)
+    cfg = cg.Config(threads_per_row=32, unroll=4, vector_width=4, split=split, dtype="f32")
+    A = D.DeviceCSR.from_host(m, "cuda", torch.float32)
+    C = D.spmm(A, torch.as_tensor(B).cuda(), sched=cg.generate("spmm", cfg)).cpu().numpy()
+    assert rel_err(C, O.spmm(m.astype(np.float64), B.astype(np.float64))) <= 1e-4
+    out = D.sddmm(A, torch.as_tensor(U).cuda(), torch.as_tensor(V).cuda(), sched=cg.generate("sddmm", cfg)).cpu().numpy()
+    assert rel_err(out, O.sddmm(m.astype(np.float64), U.astype(np.float64), V.astype(np.float64))) <= 1e-4

@@ -1,0 +1,98 @@
+"""GPU parity of the power iteration (tg_power_step_f64 & co.) against the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tilegen_b200 import lib
+from tilegen_b200 import matrices as M
+from tilegen_b200.power import PowerIteration, nnz_balanced_bounds, uniform_bounds
+
+pytestmark = pytest.mark.gpu
+
+
+def _sched(tpr=8, u=2, v=2, b=256):
+    s = lib.default_schedule()
+    s.threads_per_row, s.unroll, s.vector_width, s.block_size = tpr, u, v, b
+    return s
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-300))
+
+
+@pytest.mark.parametrize("tpr,u,v", [(4, 1, 1), (8, 2, 2), (16, 4, 2), (32, 2, 4)])
+def test_power_iteration_single_gpu_matches_oracle(tpr, u, v):
+    n = 200_000
+    A = M.c4_rows(0, n, n=n, per_row=32, seed=4)
+    x0 = np.random.default_rng(1).uniform(-1, 1, n)
+    dev = torch.device("cuda")
+    pi = PowerIteration(torch.as_tensor(A.indptr).to(dev), torch.as_tensor(A.indices).to(dev),
+                        torch.as_tensor(A.data).to(dev), uniform_bounds(n, 1), 0, sched=_sched(tpr, u, v))
+    pi.set_x0(torch.as_tensor(x0).to(dev))
+    pi.iterate(20)
+    x, lam = pi.result()
+    xr, nr = O.power_iteration(A, x0, 20)
+    assert rel(x.cpu().numpy(), xr) <= 1e-9
+    assert abs(float(lam) - nr) <= 1e-9 * nr
+
+
+@pytest.mark.parametrize("parts", [2, 3, 4, 8])
+def test_sharded_layout_emulated_on_one_gpu(parts):
+    """P shards on one device with the shard exchange done by device copies: checks the
+    nnz-balanced bounds, column renumbering, padded layout and slot reduction."""
+    A = M.baseline_matrix("c3", scale=0.3)  # power-law rows: unequal shards
+    n = A.rows
+    bounds = nnz_balanced_bounds(A.row_lengths(), parts)
+    dev = torch.device("cuda")
+    pis = []
+    for r in range(parts):
+        a, b = int(bounds[r]), int(bounds[r + 1])
+        ip = A.indptr[a:b + 1] - A.indptr[a]
+        sl = slice(int(A.indptr[a]), int(A.indptr[b]))
+        pis.append(PowerIteration(torch.as_tensor(ip).to(dev), torch.as_tensor(A.indices[sl]).to(dev),
+                                  torch.as_tensor(A.data[sl]).to(dev), bounds, r, sched=_sched(),
+                                  exchange=lambda x: None))
+    stride = pis[0].stride
+
+    def exchange(buf_index):
+        for r in range(parts):
+            src = pis[r].x[buf_index][r * stride:(r + 1) * stride]
+            for q in range(parts):
+                if q != r:
+                    pis[q].x[buf_index][r * stride:(r + 1) * stride].copy_(src)
+
+    x0 = np.random.default_rng(2).uniform(-1, 1, n)
+    for r, pi in enumerate(pis):
+        pi.set_x0(torch.as_tensor(x0[bounds[r]:bounds[r + 1]]).to(dev))
+    exchange(0)
+    cur = 0
+    for _ in range(12):
+        for pi in pis:
+            pi._step(pi.x[cur], pi.shard(pi.x[1 - cur]))
+        exchange(1 - cur)
+        cur = 1 - cur
+        for pi in pis:
+            pi.cur = cur
+    x = np.concatenate([pi.result()[0].cpu().numpy() for pi in pis])
+    xr, nr = O.power_iteration(A, x0, 12)
+    assert rel(x, xr) <= 1e-9
+    lams = [float(pi.result()[1]) for pi in pis]
+    assert max(abs(l - nr) for l in lams) <= 1e-9 * nr
+
+
+def test_power_step_is_deterministic():
+    n = 100_000
+    A = M.c4_rows(0, n, n=n, per_row=32, seed=5)
+    dev = torch.device("cuda")
+    outs = []
+    for _ in range(2):
+        pi = PowerIteration(torch.as_tensor(A.indptr).to(dev), torch.as_tensor(A.indices).to(dev),
+                            torch.as_tensor(A.data).to(dev), uniform_bounds(n, 1), 0, sched=_sched())
+        pi.set_x0(torch.ones(n, dtype=torch.float64, device=dev))
+        pi.iterate(5)
+        outs.append(pi.x[pi.cur].cpu().numpy())
+    assert np.array_equal(outs[0], outs[1])

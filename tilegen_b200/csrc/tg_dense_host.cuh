@@ -1,0 +1,207 @@
+// Host-side parameter selection and template dispatch for SpMM / SDDMM.
+//
+// Knob mapping (the reference's SpMM/SDDMM emitters only consume T, so the b200 meaning
+// of the other knobs is defined here):
+//   TPR -> G, lanes per group (clamped to 4..32 and to the lanes the row width can use),
+//   V   -> VEC, elements per gather (largest of {4,2,1} <= V that divides K and the
+//          operand alignment; 2 at most for fp64),
+//   U   -> nonzeros whose gathers are in flight per group (1, 2 or 4),
+//   B   -> threads per CTA (128, 256 or 512),
+//   split / chunk_nnz -> rowwise (one group per row) or merge (one group per chunk).
+#pragma once
+
+#include <algorithm>
+
+#include "tg_dense_ops.cuh"
+
+namespace tg {
+
+struct DenseChoice {
+    int G, VEC, NCV, U, block;
+    bool merge;
+    int64_t S;
+    int64_t ktile;  // columns per launch (SpMM column tiling)
+};
+
+inline int pow2_floor(int v) {
+    int p = 1;
+    while (p * 2 <= v) p *= 2;
+    return p;
+}
+inline int pow2_ceil(int64_t v) {
+    int p = 1;
+    while (p < v) p *= 2;
+    return p;
+}
+
+inline bool aligned_to(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+template <typename T>
+DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void* p0, const void* p1) {
+    DenseChoice d{};
+    const int vmax = sizeof(T) == 4 ? 4 : 2;
+    int vec = std::min(std::max(s.vector_width, 1), vmax);
+    vec = pow2_floor(vec);
+    while (vec > 1 && (K % vec != 0 || !aligned_to(p0, vec * sizeof(T)) || !aligned_to(p1, vec * sizeof(T))))
+        vec /= 2;
+    d.VEC = vec;
+    const int64_t nvec = (K + vec - 1) / vec;  // column vectors per row
+    int g = pow2_floor(std::min(std::max(s.threads_per_row, 4), 32));
+    g = std::max(4, std::min(g, pow2_ceil(nvec)));
+    d.G = g;
+    const int64_t per_lane = (nvec + g - 1) / g;
+    d.NCV = per_lane <= 1 ? 1 : (per_lane <= 2 ? 2 : 4);
+    d.ktile = is_spmm ? std::min<int64_t>(K, (int64_t)g * vec * d.NCV) : K;
+    d.U = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
+    d.block = (s.block_size >= 512) ? 512 : (s.block_size >= 256 ? 256 : 128);
+    d.merge = (s.split == TG_SPLIT_MERGE);
+    d.S = s.chunk_nnz > 0 ? s.chunk_nnz : 256;
+    return d;
+}
+
+template <typename T, int G, int VEC, int NCV, int U, bool MERGE>
+void launch_dense(bool is_spmm, const DenseArgs<T>& a, int block, cudaStream_t st) {
+    int64_t groups_per_block = block / G;
+    int64_t blocks = ceil_div(a.nunits, groups_per_block);
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    if (blocks < 1) blocks = 1;
+    if (is_spmm)
+        spmm_kernel<T, G, VEC, NCV, U, MERGE><<<(unsigned)blocks, block, 0, st>>>(a);
+    else
+        sddmm_kernel<T, G, VEC, NCV, U, MERGE><<<(unsigned)blocks, block, 0, st>>>(a);
+}
+
+template <typename T, int G, int VEC, int NCV, int U>
+bool dense_m(const DenseChoice& d, bool sp, const DenseArgs<T>& a, cudaStream_t st) {
+    if (d.merge)
+        launch_dense<T, G, VEC, NCV, U, true>(sp, a, d.block, st);
+    else
+        launch_dense<T, G, VEC, NCV, U, false>(sp, a, d.block, st);
+    return true;
+}
+
+template <typename T, int G, int VEC, int NCV>
+bool dense_u(const DenseChoice& d, bool sp, const DenseArgs<T>& a, cudaStream_t st) {
+    switch (d.U) {
+        case 1: return dense_m<T, G, VEC, NCV, 1>(d, sp, a, st);
+        case 2: return dense_m<T, G, VEC, NCV, 2>(d, sp, a, st);
+        case 4: return dense_m<T, G, VEC, NCV, 4>(d, sp, a, st);
+    }
+    return false;
+}
+
+template <typename T, int G, int VEC>
+bool dense_n(const DenseChoice& d, bool sp, const DenseArgs<T>& a, cudaStream_t st) {
+    switch (d.NCV) {
+        case 1: return dense_u<T, G, VEC, 1>(d, sp, a, st);
+        case 2: return dense_u<T, G, VEC, 2>(d, sp, a, st);
+        case 4: return dense_u<T, G, VEC, 4>(d, sp, a, st);
+    }
+    return false;
+}
+
+template <typename T, int G>
+bool dense_v(const DenseChoice& d, bool sp, const DenseArgs<T>& a, cudaStream_t st) {
+    switch (d.VEC) {
+        case 1: return dense_n<T, G, 1>(d, sp, a, st);
+        case 2: return dense_n<T, G, 2>(d, sp, a, st);
+        case 4:
+            if constexpr (sizeof(T) == 4) return dense_n<T, G, 4>(d, sp, a, st);
+            return false;
+    }
+    return false;
+}
+
+template <typename T>
+bool dense_dispatch(const DenseChoice& d, bool sp, const DenseArgs<T>& a, cudaStream_t st) {
+    switch (d.G) {
+        case 4: return dense_v<T, 4>(d, sp, a, st);
+        case 8: return dense_v<T, 8>(d, sp, a, st);
+        case 16: return dense_v<T, 16>(d, sp, a, st);
+        case 32: return dense_v<T, 32>(d, sp, a, st);
+    }
+    return false;
+}
+
+template <typename T>
+size_t dense_ws_bytes(int64_t rows, int64_t nnz, int64_t K, const tg_sched& s, bool is_spmm) {
+    (void)rows;
+    if (s.split != TG_SPLIT_MERGE || nnz <= 0 || K <= 0) return 0;
+    // alignment does not change the partial width's upper bound: size for the widest tile
+    const DenseChoice d = choose_dense<T>(s, K, is_spmm, nullptr, nullptr);
+    const int64_t nchunks = ceil_div(nnz, d.S);
+    const int64_t width = is_spmm ? (int64_t)d.G * (sizeof(T) == 4 ? 4 : 2) * 4 : 0;
+    return split_ws_bytes(nchunks, width, sizeof(T));
+}
+
+// C = A * B (SpMM) or out = A .* (U V^T) on A's pattern (SDDMM, B = V).
+template <typename T>
+int dense_run(bool is_spmm, const tg_csr& A, const T* B, const T* U, T* C, int64_t K, const tg_sched& s, void* ws,
+              size_t ws_bytes, cudaStream_t st) {
+    if (K <= 0) return set_error(TG_EINVAL, "dense width K must be positive (got %lld)", (long long)K);
+    if (A.rows == 0) return TG_OK;
+    const DenseChoice d = choose_dense<T>(s, K, is_spmm, B, is_spmm ? (const void*)C : (const void*)U);
+    DenseArgs<T> a{};
+    a.indptr = A.indptr;
+    a.indices = A.indices;
+    a.data = static_cast<const T*>(A.data);
+    a.rows = A.rows;
+    a.nnz = A.nnz;
+    a.ld = K;
+    a.row_limit = (s.flags & TG_FLAG_INJECT_BUG) ? A.rows - 1 : A.rows;
+    a.S = d.S;
+    if (!is_spmm && A.nnz == 0) return TG_OK;
+    if (d.merge && A.nnz > 0) {
+        const int64_t nchunks = ceil_div(A.nnz, d.S);
+        const int64_t width = is_spmm ? (int64_t)d.G * (sizeof(T) == 4 ? 4 : 2) * 4 : 0;
+        const size_t need = split_ws_bytes(nchunks, width, sizeof(T));
+        if (ws == nullptr || ws_bytes < need)
+            return set_error(TG_ENOMEM, "%s merge split needs %zu workspace bytes, got %zu", is_spmm ? "spmm" : "sddmm",
+                             need, ws_bytes);
+        SplitWs w = split_ws_carve(ws, nchunks, width, sizeof(T));
+        int rc = launch_partition(A.indptr, A.rows, A.nnz, d.S, w, st);
+        if (rc != TG_OK) return rc;
+        a.own_first = w.own_first;
+        a.cnt = w.cnt;
+        a.head = static_cast<T*>(w.head);
+        a.tail = static_cast<T*>(w.tail);
+        a.nunits = nchunks;
+        a.kpart = (int64_t)d.G * d.VEC * d.NCV;
+    } else {
+        DenseChoice dr = d;
+        dr.merge = false;
+        a.nunits = A.rows;
+        a.kpart = (int64_t)d.G * d.VEC * d.NCV;
+        if (is_spmm && A.nnz == 0) {
+            // every row is empty: C = 0 through the rowwise kernel (it writes empty rows)
+        }
+        for (int64_t k0 = 0; k0 < (is_spmm ? K : 1); k0 += d.ktile) {
+            DenseArgs<T> t = a;
+            t.B = B + (is_spmm ? k0 : 0);
+            t.U = U;
+            t.C = C + (is_spmm ? k0 : 0);
+            t.kt = is_spmm ? std::min(d.ktile, K - k0) : K;
+            if (!dense_dispatch<T>(dr, is_spmm, t, st))
+                return set_error(TG_EUNSUPPORTED, "no %s instance for G=%d VEC=%d NCV=%d U=%d",
+                                 is_spmm ? "spmm" : "sddmm", d.G, d.VEC, d.NCV, d.U);
+            int rc = check_launch(is_spmm ? "spmm_kernel" : "sddmm_kernel");
+            if (rc != TG_OK) return rc;
+        }
+        return TG_OK;
+    }
+    for (int64_t k0 = 0; k0 < (is_spmm ? K : 1); k0 += d.ktile) {
+        DenseArgs<T> t = a;
+        t.B = B + (is_spmm ? k0 : 0);
+        t.U = U;
+        t.C = C + (is_spmm ? k0 : 0);
+        t.kt = is_spmm ? std::min(d.ktile, K - k0) : K;
+        if (!dense_dispatch<T>(d, is_spmm, t, st))
+            return set_error(TG_EUNSUPPORTED, "no %s instance for G=%d VEC=%d NCV=%d U=%d", is_spmm ? "spmm" : "sddmm",
+                             d.G, d.VEC, d.NCV, d.U);
+        int rc = check_launch(is_spmm ? "spmm_kernel" : "sddmm_kernel");
+        if (rc != TG_OK) return rc;
+    }
+    return TG_OK;
+}
+
+}  // namespace tg

@@ -1,0 +1,81 @@
+// Row dot product of the rowwise split, shared by SpMV (tg_spmv.cu) and the power
+// iteration (tg_power.cu): TPR lanes of a group stride over the row, each lane keeps U
+// vector loads of V nonzeros in flight (indices/values streamed with an L2 evict_first
+// policy, x gathered with evict_last), with a scalar peel to the V-element boundary and
+// a ragged scalar tail.
+#pragma once
+
+#include "tg_common.cuh"
+
+namespace tg {
+
+template <typename T, int V>
+__device__ __forceinline__ void ld_stream_vec(const int64_t* pi, const T* pv, uint64_t pol, int64_t (&c)[V],
+                                              T (&v)[V]) {
+    if constexpr (V == 1) {
+        c[0] = ld_stream(pi, pol);
+        v[0] = ld_stream(pv, pol);
+    } else {
+#pragma unroll
+        for (int e = 0; e < V; e += 2) ld_stream2(pi + e, pol, c[e], c[e + 1]);
+#pragma unroll
+        for (int e = 0; e < V; e += 2) ld_stream2(pv + e, pol, v[e], v[e + 1]);
+    }
+}
+
+// Dot product of row [p, pe) with x by the TPR lanes of one group (this lane's share).
+template <typename T, int TPR, int U, int V>
+__device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* __restrict__ val,
+                                     const T* __restrict__ x, int64_t p, int64_t pe, int lane, uint64_t ps,
+                                     uint64_t pg) {
+    T acc = T(0);
+    if constexpr (V == 1) {
+        int64_t q = p + lane;
+        for (; q + (int64_t)(U - 1) * TPR < pe; q += (int64_t)TPR * U) {
+            int64_t c[U];
+            T v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                c[u] = ld_stream(idx + q + u * TPR, ps);
+                v[u] = ld_stream(val + q + u * TPR, ps);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) acc = fma(v[u], ld_gather(x + c[u], pg), acc);
+        }
+        for (; q < pe; q += TPR) acc = fma(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg), acc);
+    } else {
+        // peel to a V-element boundary, full vectors, then the ragged tail
+        int64_t pa = (p + V - 1) / V * V;
+        if (pa > pe) pa = pe;
+        for (int64_t q = p + lane; q < pa; q += TPR)
+            acc = fma(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg), acc);
+        const int64_t nv = (pe - pa) / V;
+        int64_t k = lane;
+        for (; k + (int64_t)(U - 1) * TPR < nv; k += (int64_t)TPR * U) {
+            int64_t c[U][V];
+            T v[U][V];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t q = pa + (k + (int64_t)u * TPR) * V;
+                ld_stream_vec<T, V>(idx + q, val + q, ps, c[u], v[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int e = 0; e < V; ++e) acc = fma(v[u][e], ld_gather(x + c[u][e], pg), acc);
+        }
+        for (; k < nv; k += TPR) {
+            int64_t c[V];
+            T v[V];
+            const int64_t q = pa + k * V;
+            ld_stream_vec<T, V>(idx + q, val + q, ps, c, v);
+#pragma unroll
+            for (int e = 0; e < V; ++e) acc = fma(v[e], ld_gather(x + c[e], pg), acc);
+        }
+        for (int64_t q = pa + nv * V + lane; q < pe; q += TPR)
+            acc = fma(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg), acc);
+    }
+    return acc;
+}
+
+}  // namespace tg

@@ -1,0 +1,188 @@
+"""Row-sharded power iteration x <- A x / ||A x|| on one GPU per process.
+
+The multi-GPU mode of the hot path (no counterpart in the reference, whose kernels run on
+one device).  Rows of A are split into P contiguous, nnz-balanced shards, one per rank;
+x is replicated.  The iterate lives in a padded vector of P * stride doubles (shard r at
+r * stride, its sum of squares in the shard's last element, the slot -- see
+include/tilegen_b200.h), and the column indices of each shard are renumbered once to that
+layout, so the all-gather of the output shards *is* the next iterate: no compaction, no
+separate norm all-reduce (every rank sums the P slots it received), and the 1/||y|| scale
+is applied inside the next step's kernel.
+
+``PowerIteration`` drives one rank.  Its exchange step is pluggable: by default an
+in-place ``torch.distributed.all_gather_into_tensor`` (NCCL over NVLink/NVSwitch), no
+exchange at P = 1.  The local step is the C ABI's ``tg_power_step_f64``; tests on CPU
+substitute a host implementation of the same contract.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+__all__ = ["nnz_balanced_bounds", "uniform_bounds", "padded_stride", "renumber_columns", "PowerIteration"]
+
+
+def nnz_balanced_bounds(row_nnz: np.ndarray, parts: int) -> np.ndarray:
+    """Row boundaries b[0..parts] so rank r owns rows [b[r], b[r+1]) with about nnz/parts
+    nonzeros each: b[r] is the first row whose nnz prefix reaches r * nnz / parts."""
+    if parts < 1:
+        raise ValueError("parts must be >= 1")
+    csum = np.concatenate([[0], np.cumsum(np.asarray(row_nnz, dtype=np.int64))])
+    total = int(csum[-1])
+    rows = csum.size - 1
+    b = np.empty(parts + 1, dtype=np.int64)
+    b[0], b[parts] = 0, rows
+    for r in range(1, parts):
+        b[r] = int(np.searchsorted(csum, (r * total) // parts, side="left"))
+    return np.maximum.accumulate(b)
+
+
+def uniform_bounds(rows: int, parts: int) -> np.ndarray:
+    """Equal row blocks (the nnz-balanced split of a constant-row-length matrix)."""
+    return np.array([(r * rows) // parts for r in range(parts + 1)], dtype=np.int64)
+
+
+def padded_stride(bounds: np.ndarray, align: int = 32) -> int:
+    """Shard stride: the largest shard plus one slot, rounded up to `align` doubles."""
+    longest = int(np.max(np.diff(bounds))) if bounds.size > 1 else 0
+    return ((longest + 1 + align - 1) // align) * align
+
+
+def renumber_columns(indices, bounds, stride: int):
+    """j -> owner(j) * stride + (j - bounds[owner(j)]), on numpy or torch tensors."""
+    try:
+        import torch
+
+        if isinstance(indices, torch.Tensor):
+            b = torch.as_tensor(bounds, dtype=torch.int64, device=indices.device)
+            owner = torch.searchsorted(b, indices, right=True) - 1
+            return owner * stride + (indices - b[owner])
+    except ImportError:  # pragma: no cover
+        pass
+    b = np.asarray(bounds, dtype=np.int64)
+    owner = np.searchsorted(b, indices, side="right") - 1
+    return owner * stride + (indices - b[owner])
+
+
+class PowerIteration:
+    """One rank of the sharded power iteration.
+
+    Parameters: the rank's CSR shard on its device as torch tensors (indptr rebased to 0,
+    ORIGINAL global column indices), the global row bounds, this rank, and optionally a
+    custom ``step`` (signature ``step(x_full, y_shard)``), ``norm2`` (``norm2(shard)``),
+    ``finalize`` (``finalize(x_full, x_out, lam_out)``) and ``exchange``
+    (``exchange(x_full)``, all-gathers the shards in place).  The custom hooks exist for
+    host-side tests of the sharding logic; the defaults are the GPU kernels.
+    """
+
+    def __init__(self, indptr, indices, data, bounds: Sequence[int], rank: int, sched=None,
+                 step: Optional[Callable] = None, norm2: Optional[Callable] = None,
+                 finalize: Optional[Callable] = None, exchange: Optional[Callable] = None,
+                 renumber: bool = True):
+        import torch
+
+        self.torch = torch
+        self.bounds = np.asarray(bounds, dtype=np.int64)
+        self.parts = int(self.bounds.size - 1)
+        self.rank = int(rank)
+        self.rows = int(self.bounds[rank + 1] - self.bounds[rank])
+        self.cols = int(self.bounds[-1])
+        self.stride = padded_stride(self.bounds)
+        self.device = indptr.device
+        if int(indptr.numel()) != self.rows + 1:
+            raise ValueError("indptr has %d entries for a %d-row shard" % (indptr.numel(), self.rows))
+        self.indptr = indptr
+        self.indices = renumber_columns(indices, self.bounds, self.stride) if renumber else indices
+        self.data = data
+        self.nnz = int(indices.numel())
+        n = self.parts * self.stride
+        self.x = [torch.zeros(n, dtype=torch.float64, device=self.device) for _ in range(2)]
+        self.cur = 0
+        self.sched = sched
+        self._step = step or self._gpu_step
+        self._norm2 = norm2 or self._gpu_norm2
+        self._finalize = finalize or self._gpu_finalize
+        self._exchange = exchange or (self._nccl_exchange if self.parts > 1 else (lambda x: None))
+        self.kernel_launches = 0
+        if step is None or norm2 is None or finalize is None:
+            from . import lib as _lib
+
+            self._lib = _lib
+            L = _lib.load()
+            self.ws = torch.zeros(int(L.tg_power_workspace_bytes()), dtype=torch.uint8, device=self.device)
+            self._desc = _lib.TgCsr(self.rows, n, self.nnz, self.indptr.data_ptr(), self.indices.data_ptr(),
+                                    self.data.data_ptr())
+            self._sched_c = sched if sched is not None else self._default_sched()
+
+    # -- shard views -------------------------------------------------------------------
+    def shard(self, buf) -> "object":
+        o = self.rank * self.stride
+        return buf[o:o + self.stride]
+
+    # -- GPU implementations -----------------------------------------------------------
+    def _default_sched(self):
+        s = self._lib.default_schedule()
+        s.threads_per_row, s.unroll, s.vector_width, s.block_size, s.tile = 8, 2, 2, 256, 32
+        return s
+
+    def _stream(self) -> int:
+        return int(self.torch.cuda.current_stream(self.device).cuda_stream)
+
+    def _gpu_step(self, x_full, y_shard) -> None:
+        L = self._lib.load()
+        self._lib.check(L.tg_power_step_f64(ctypes.byref(self._desc), x_full.data_ptr(), self.parts, self.stride,
+                                            y_shard.data_ptr(), ctypes.byref(self._sched_c), self.ws.data_ptr(),
+                                            self.ws.numel(), self._stream()), "tg_power_step_f64")
+        self.kernel_launches += 1
+
+    def _gpu_norm2(self, shard) -> None:
+        L = self._lib.load()
+        self._lib.check(L.tg_shard_norm2_f64(shard.data_ptr(), self.rows, self.stride, self.ws.data_ptr(),
+                                             self.ws.numel(), self._stream()), "tg_shard_norm2_f64")
+        self.kernel_launches += 1
+
+    def _nccl_exchange(self, x_full) -> None:
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(x_full, self.shard(x_full))
+
+    # -- iteration ---------------------------------------------------------------------
+    def set_x0(self, x0_local) -> None:
+        """Start from x0 (this rank's rows); any scale (the first step normalises)."""
+        xs = self.shard(self.x[0])
+        xs.zero_()
+        xs[:self.rows].copy_(x0_local)
+        self._norm2(xs)
+        self._exchange(self.x[0])
+        self.cur = 0
+
+    def iterate(self, iters: int, on_step: Optional[Callable[[int], None]] = None) -> None:
+        for k in range(iters):
+            src, dst = self.x[self.cur], self.x[1 - self.cur]
+            if on_step:
+                on_step(2 * k)
+            self._step(src, self.shard(dst))
+            if on_step:
+                on_step(2 * k + 1)
+            self._exchange(dst)
+            self.cur = 1 - self.cur
+
+    def _gpu_finalize(self, x_full, x_out, lam_out) -> None:
+        L = self._lib.load()
+        self._lib.check(L.tg_power_finalize_f64(x_full.data_ptr(), self.parts, self.stride, self.rank, self.rows,
+                                                x_out.data_ptr(), lam_out.data_ptr(), self._stream()),
+                        "tg_power_finalize_f64")
+        self.kernel_launches += 1
+
+    def result(self, x_out=None, lam_out=None) -> Tuple[object, object]:
+        """(this rank's rows of the normalised iterate, ||A x_prev||) as tensors."""
+        torch = self.torch
+        if x_out is None:
+            x_out = torch.empty(self.rows, dtype=torch.float64, device=self.device)
+        if lam_out is None:
+            lam_out = torch.empty(1, dtype=torch.float64, device=self.device)
+        self._finalize(self.x[self.cur], x_out, lam_out)
+        return x_out, lam_out
