@@ -45,13 +45,14 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--rows", type=int, default=C4_N, help="matrix size (default: the C4 config)")
     ap.add_argument("--iters", type=int, default=ITERS)
     ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--tpr", type=int, default=8)
+    ap.add_argument("--split", choices=["stream", "rowwise"], default="rowwise")
+    ap.add_argument("--tpr", type=int, default=4)
     ap.add_argument("--unroll", type=int, default=2)
     ap.add_argument("--vec", type=int, default=2)
     ap.add_argument("--block", type=int, default=256)
@@ -98,7 +99,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.FIELDS,
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -281,6 +282,7 @@ def main():
 
     s = lib.default_schedule()
     s.threads_per_row, s.unroll, s.vector_width, s.block_size, s.tile = args.tpr, args.unroll, args.vec, args.block, 32
+    s.split = lib.TG_SPLIT_STREAM if args.split == "stream" else lib.TG_SPLIT_ROWWISE
     lib.validate_schedule(s)
 
     d_ip = h_ip.to(dev)
@@ -337,7 +339,7 @@ def main():
 
     # ---- e2e through the public API from pinned host buffers
     e2e_ms = []
-    for it in range(args.e2e_steps + 1):
+    for it in range(args.e2e_steps + 1 if args.e2e_steps > 0 else 0):
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -358,7 +360,7 @@ def main():
         if it > 0:  # the first pass warms allocator and communicator buffers
             e2e_ms.append(e0.elapsed_time(e1))
         del pe, ip, dd, xx
-    e2e_local = float(np.mean(e2e_ms))
+    e2e_local = float(np.mean(e2e_ms)) if e2e_ms else float("nan")
 
     # ---- max over ranks
     vals = torch.tensor([ms_local, k_ms_local, e2e_local], dtype=torch.float64, device=dev)
@@ -374,11 +376,12 @@ def main():
         peak, peak_kind = measured_peaks()
         local_bytes = spmv_bytes(r1 - r0, n, shard.nnz)
         achieved = local_bytes / (k_ms / 1e3) / 1e9
-        tr = traffic_record("c4_%d" % world, "power_step_kernel")
+        kname = "spmv_stream_kernel(power)" if args.split == "stream" else "power_step_kernel"
+        tr = traffic_record("c4_%d" % world, kname)
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(achieved / peak, 4), "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"
                     if peak_kind == "measured" else "fallback 6.65 TB/s",
-                    "kernel": "power_step_kernel", "kernel_ms": round(k_ms, 4),
+                    "kernel": kname, "kernel_ms": round(k_ms, 4),
                     "algorithmic_bytes_per_launch": local_bytes,
                     "traffic": tr["dram_bytes_per_launch"] if tr else None}
         line = {
@@ -402,7 +405,8 @@ def main():
             "roofline": roofline,
             "clocks": clocks,
             "wall_s_timed": round(wall, 4),
-            "schedule": {"tpr": args.tpr, "unroll": args.unroll, "vec": args.vec, "block": args.block},
+            "schedule": {"split": args.split, "tpr": args.tpr, "unroll": args.unroll, "vec": args.vec,
+                         "block": args.block},
             "lambda": float(h_lam[0]),
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -60,11 +60,15 @@ typedef void* tg_stream_t;
 /* Row-to-thread mapping of the kernels. */
 #define TG_SPLIT_ROWWISE 0 /* reference mapping: T rows per CTA tile, TPR lanes per row */
 #define TG_SPLIT_MERGE 1   /* nnz-balanced chunks, rows split across chunks + fix-up */
-#define TG_SPLIT_AUTO 2    /* library picks from the row-length statistics */
+#define TG_SPLIT_AUTO 2    /* library picks (stream when the operands allow it) */
+#define TG_SPLIT_STREAM 3  /* SpMV: persistent TMA-fed streaming kernel (nnz-balanced chunks) */
 
 /* flags */
 #define TG_FLAG_BOUNDS_CHECK 1u /* validate indptr/indices on the device; TG_EBOUNDS on error */
 #define TG_FLAG_INJECT_BUG 2u   /* deliberately skip the last row (harness self-test) */
+#define TG_FLAG_REUSE_PLAN 4u   /* stream split: the workspace already holds this matrix's
+                                   partition from an earlier call with the same A and
+                                   schedule; skip the analysis pass */
 
 /*
  * Mirrors tilegen.codegen.Lowering (tilegen/codegen.py:90-134): each knob of the
@@ -155,7 +159,7 @@ TG_API int tg_axpy_f64(const double* x, const double* w, double* z, double alpha
  * holds sum(shard^2).  A's column indices must be renumbered to this layout
  * (j -> owner(j) * stride + j - first_row(owner)).  The workspace must be zero-filled
  * before its first use; every call leaves it zeroed. */
-TG_API size_t tg_power_workspace_bytes(void);
+TG_API size_t tg_power_workspace_bytes(int64_t nnz, const tg_sched* s);
 /* y[0..rows) = A x / sqrt(sum of the nparts slots of x); y[stride-1] = sum(y^2). */
 TG_API int tg_power_step_f64(const tg_csr* A, const double* x, int32_t nparts, int64_t stride,
                              double* y, const tg_sched* s, void* workspace,

@@ -45,10 +45,15 @@ B200_SCHEDULES = [
     cg.Config(split="merge", block_size=128, threads_per_row=8, unroll=4, vector_width=4, chunk_nnz=64),
     cg.Config(split="merge", block_size=512, threads_per_row=32, unroll=2, vector_width=2, chunk_nnz=16),
     cg.Config(tile_size=64, threads_per_row=16, unroll=4, vector_width=4, block_size=256),
+    cg.Config(split="stream", unroll=1, block_size=256),
+    cg.Config(split="stream", unroll=2, block_size=256),
+    cg.Config(split="stream", unroll=4, block_size=128),
+    cg.Config(split="stream", unroll=8, block_size=256),
 ]
 ALL = REF_SCHEDULES + B200_SCHEDULES
 IDS = ["%s-T%d-TPR%d-U%d-V%d-B%d" % (c.split, c.tile_size, c.threads_per_row, c.unroll, c.vector_width, c.block_size)
        for c in ALL]
+STREAM = [c for c in B200_SCHEDULES if c.split == "stream"]
 
 
 def rel_err(out, ref):
@@ -93,7 +98,7 @@ def test_fp32_accumulation_within_1e_4(kernel, cfg, edge, edge_csr):
 
 
 @pytest.mark.parametrize("kernel", KERNELS)
-@pytest.mark.parametrize("split", ["rowwise", "merge"])
+@pytest.mark.parametrize("split", ["rowwise", "merge", "stream"])
 def test_injected_bug_is_caught(kernel, split, edge_csr):
     cfg = cg.Config(tile_size=32, threads_per_row=4, unroll=2, vector_width=1, block_size=256, inject_bug=True,
                     split=split)
@@ -114,7 +119,7 @@ def test_reference_abi_launchers(kernel, cfg, edge, edge_csr):
     lib.set_schedule(lib.default_schedule())
 
 
-@pytest.mark.parametrize("split", ["rowwise", "merge"])
+@pytest.mark.parametrize("split", ["rowwise", "merge", "stream"])
 def test_corner_cases(corner, split):
     for name in ("bug4", "empty_row3", "zeros2", "small3"):
         shape = tuple(int(s) for s in corner[name + "_shape"])
@@ -128,7 +133,7 @@ def test_corner_cases(corner, split):
             assert np.all(out == 0.0)  # exact zero (tests/test_verify.py:39-43)
 
 
-@pytest.mark.parametrize("split", ["rowwise", "merge"])
+@pytest.mark.parametrize("split", ["rowwise", "merge", "stream"])
 def test_empty_and_degenerate_shapes(split):
     dev = torch.device("cuda")
     s = cg.generate("spmv", cg.Config(split=split)).sched
@@ -151,7 +156,8 @@ def test_empty_and_degenerate_shapes(split):
 
 @pytest.mark.parametrize("cls", M.corpus_classes())
 @pytest.mark.parametrize("cfg", [cg.Config(threads_per_row=8, unroll=2, vector_width=2, block_size=256),
-                                 cg.Config(split="merge", block_size=256)], ids=["TPR8", "merge"])
+                                 cg.Config(split="merge", block_size=256),
+                                 cg.Config(split="stream", unroll=2)], ids=["TPR8", "merge", "stream"])
 def test_corpus_classes_spmv_full(cls, cfg):
     m = M.make_matrix(cls)
     x = inputs_for("spmv", m, 8, 7)[0]
@@ -161,7 +167,9 @@ def test_corpus_classes_spmv_full(cls, cfg):
 
 @pytest.mark.parametrize("name", ["c1", "c2", "c3"])
 @pytest.mark.parametrize("cfg", [cg.Config(tile_size=64, threads_per_row=16, unroll=2, vector_width=2, block_size=256),
-                                 cg.Config(split="merge", block_size=256)], ids=["TPR16", "merge"])
+                                 cg.Config(split="merge", block_size=256),
+                                 cg.Config(split="stream", unroll=1),
+                                 cg.Config(split="stream", unroll=8)], ids=["TPR16", "merge", "stream1", "stream8"])
 def test_baseline_spmv_configs_full_size(name, cfg):
     m = M.baseline_matrix(name)
     x = np.random.default_rng(11).uniform(-1, 1, m.cols)
@@ -186,8 +194,9 @@ def _long_row_matrix():
 
 @pytest.mark.parametrize("cfg", [cg.Config(split="merge", block_size=128), cg.Config(split="merge", block_size=256),
                                  cg.Config(split="merge", threads_per_row=32, unroll=4, vector_width=2, chunk_nnz=32),
-                                 cg.Config(threads_per_row=32, unroll=4, vector_width=2)],
-                         ids=["merge128", "merge256", "merge-c32", "rowwise"])
+                                 cg.Config(threads_per_row=32, unroll=4, vector_width=2),
+                                 cg.Config(split="stream", unroll=1), cg.Config(split="stream", unroll=8)],
+                         ids=["merge128", "merge256", "merge-c32", "rowwise", "stream1", "stream8"])
 def test_long_rows_spanning_chunks(cfg):
     m = _long_row_matrix()
     data = inputs_for("spmm", m, 16, 3)
@@ -207,6 +216,26 @@ def test_merge_results_are_deterministic():
     assert np.array_equal(a, b)
     g = cg.generate("spmm", cg.Config(split="merge", chunk_nnz=32))
     assert np.array_equal(run_kernel(g, m, data, K=16), run_kernel(g, m, data, K=16))
+    g = cg.generate("spmv", cg.Config(split="stream", unroll=2))
+    assert np.array_equal(run_kernel(g, m, data), run_kernel(g, m, data))
+
+
+def test_stream_plan_reuse_flag():
+    """TG_FLAG_REUSE_PLAN skips the analysis pass on a workspace planned for the same
+    matrix; results are identical to a planned call."""
+    m = _long_row_matrix()
+    A = D.DeviceCSR.from_host(m, "cuda")
+    x = torch.as_tensor(np.random.default_rng(3).uniform(-1, 1, m.cols)).cuda()
+    s = cg.generate("spmv", cg.Config(split="stream", unroll=4)).sched
+    L = lib.load()
+    nb = L.tg_spmv_workspace_bytes(m.rows, m.nnz, ctypes.byref(s))
+    ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    y1 = D.spmv(A, x, sched=s, workspace=ws)
+    s.flags |= lib.TG_FLAG_REUSE_PLAN
+    y2 = D.spmv(A, x, sched=s, workspace=ws)
+    y3 = D.spmv(A, x, sched=s, workspace=ws)
+    assert torch.equal(y1, y2) and torch.equal(y2, y3)
+    check_f64(y1.cpu().numpy(), O.spmv(m, x.cpu().numpy()), m)
 
 
 @pytest.mark.parametrize("K", [1, 3, 8, 64, 100, 128, 600])

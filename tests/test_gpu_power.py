@@ -14,9 +14,10 @@ from tilegen_b200.power import PowerIteration, nnz_balanced_bounds, uniform_boun
 pytestmark = pytest.mark.gpu
 
 
-def _sched(tpr=8, u=2, v=2, b=256):
+def _sched(tpr=8, u=2, v=2, b=256, split="rowwise"):
     s = lib.default_schedule()
     s.threads_per_row, s.unroll, s.vector_width, s.block_size = tpr, u, v, b
+    s.split = lib.TG_SPLIT_STREAM if split == "stream" else lib.TG_SPLIT_ROWWISE
     return s
 
 
@@ -24,14 +25,16 @@ def rel(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-300))
 
 
-@pytest.mark.parametrize("tpr,u,v", [(4, 1, 1), (8, 2, 2), (16, 4, 2), (32, 2, 4)])
-def test_power_iteration_single_gpu_matches_oracle(tpr, u, v):
+@pytest.mark.parametrize("tpr,u,v,split", [(4, 1, 1, "rowwise"), (8, 2, 2, "rowwise"), (16, 4, 2, "rowwise"),
+                                           (32, 2, 4, "rowwise"), (4, 1, 1, "stream"), (4, 2, 2, "stream"),
+                                           (4, 4, 2, "stream"), (4, 8, 2, "stream")])
+def test_power_iteration_single_gpu_matches_oracle(tpr, u, v, split):
     n = 200_000
     A = M.c4_rows(0, n, n=n, per_row=32, seed=4)
     x0 = np.random.default_rng(1).uniform(-1, 1, n)
     dev = torch.device("cuda")
     pi = PowerIteration(torch.as_tensor(A.indptr).to(dev), torch.as_tensor(A.indices).to(dev),
-                        torch.as_tensor(A.data).to(dev), uniform_bounds(n, 1), 0, sched=_sched(tpr, u, v))
+                        torch.as_tensor(A.data).to(dev), uniform_bounds(n, 1), 0, sched=_sched(tpr, u, v, 256, split))
     pi.set_x0(torch.as_tensor(x0).to(dev))
     pi.iterate(20)
     x, lam = pi.result()
@@ -41,7 +44,8 @@ def test_power_iteration_single_gpu_matches_oracle(tpr, u, v):
 
 
 @pytest.mark.parametrize("parts", [2, 3, 4, 8])
-def test_sharded_layout_emulated_on_one_gpu(parts):
+@pytest.mark.parametrize("split", ["rowwise", "stream"])
+def test_sharded_layout_emulated_on_one_gpu(parts, split):
     """P shards on one device with the shard exchange done by device copies: checks the
     nnz-balanced bounds, column renumbering, padded layout and slot reduction."""
     A = M.baseline_matrix("c3", scale=0.3)  # power-law rows: unequal shards
@@ -54,7 +58,7 @@ def test_sharded_layout_emulated_on_one_gpu(parts):
         ip = A.indptr[a:b + 1] - A.indptr[a]
         sl = slice(int(A.indptr[a]), int(A.indptr[b]))
         pis.append(PowerIteration(torch.as_tensor(ip).to(dev), torch.as_tensor(A.indices[sl]).to(dev),
-                                  torch.as_tensor(A.data[sl]).to(dev), bounds, r, sched=_sched(),
+                                  torch.as_tensor(A.data[sl]).to(dev), bounds, r, sched=_sched(split=split),
                                   exchange=lambda x: None))
     stride = pis[0].stride
 
@@ -84,14 +88,15 @@ def test_sharded_layout_emulated_on_one_gpu(parts):
     assert max(abs(l - nr) for l in lams) <= 1e-9 * nr
 
 
-def test_power_step_is_deterministic():
+@pytest.mark.parametrize("split", ["rowwise", "stream"])
+def test_power_step_is_deterministic(split):
     n = 100_000
     A = M.c4_rows(0, n, n=n, per_row=32, seed=5)
     dev = torch.device("cuda")
     outs = []
     for _ in range(2):
         pi = PowerIteration(torch.as_tensor(A.indptr).to(dev), torch.as_tensor(A.indices).to(dev),
-                            torch.as_tensor(A.data).to(dev), uniform_bounds(n, 1), 0, sched=_sched())
+                            torch.as_tensor(A.data).to(dev), uniform_bounds(n, 1), 0, sched=_sched(split=split))
         pi.set_x0(torch.ones(n, dtype=torch.float64, device=dev))
         pi.iterate(5)
         outs.append(pi.x[pi.cur].cpu().numpy())

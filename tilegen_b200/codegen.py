@@ -62,7 +62,8 @@ STANDARD_KERNELS: Dict[str, str] = {
 # Kernels whose statements contain a rank-2 dense access (the only ones the reference's
 # vectorize pass keeps Vectorize for, tilegen/passes.py:348-396).
 _HAS_2D_DENSE = {"spmm", "sddmm"}
-_SPLITS = {"rowwise": _lib.TG_SPLIT_ROWWISE, "merge": _lib.TG_SPLIT_MERGE, "auto": _lib.TG_SPLIT_AUTO}
+_SPLITS = {"rowwise": _lib.TG_SPLIT_ROWWISE, "merge": _lib.TG_SPLIT_MERGE, "auto": _lib.TG_SPLIT_AUTO,
+           "stream": _lib.TG_SPLIT_STREAM}
 
 
 @dataclass
@@ -70,7 +71,8 @@ class Config:
     """Schedule knobs (tilegen/codegen.py:61-87) plus the b200-only ones.
 
     ``split`` chooses the row mapping of the b200 kernels ("rowwise": the reference's
-    T/TPR mapping; "merge": nnz-balanced chunks), ``chunk_nnz`` the merge chunk size for
+    T/TPR mapping; "merge": nnz-balanced chunks; "stream": the persistent TMA-fed SpMV,
+    merge for SpMM/SDDMM; "auto": stream), ``chunk_nnz`` the merge chunk size for
     SpMM/SDDMM, ``bounds_check`` a device-side CSR validation before the call."""
 
     tile_size: int = 32

@@ -44,7 +44,7 @@ size_t spmv_ws_bytes(int64_t rows, int64_t nnz, const tg_sched& s, size_t elem);
 int axpy_run(const double* x, const double* w, double* z, double alpha, double beta, int64_t n, int block,
              cudaStream_t st);
 // power iteration (tg_power.cu)
-size_t power_ws_bytes();
+size_t power_ws_bytes(int64_t nnz, const tg_sched& s);
 int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride, double* y, const tg_sched& s,
                    void* ws, size_t ws_bytes, cudaStream_t st);
 int shard_norm2_run(double* shard, int64_t rows, int64_t stride, void* ws, size_t ws_bytes, cudaStream_t st);
@@ -105,7 +105,7 @@ int resolve(const tg_sched* in, tg_sched* out) {
     if (s.unroll <= 0) s.unroll = 1;
     if (s.vector_width <= 0) s.vector_width = 1;
     if (s.block_size <= 0) s.block_size = 128;
-    if (s.split == TG_SPLIT_AUTO) s.split = TG_SPLIT_MERGE;
+    if (s.split == TG_SPLIT_AUTO) s.split = TG_SPLIT_STREAM;
     const int tpr = s.threads_per_row;
     if (tpr != 1 && tpr != 2 && tpr != 4 && tpr != 8 && tpr != 16 && tpr != 32)
         return set_error(TG_EINVAL, "threads_per_row must be 1, 2, 4, 8, 16 or 32 (got %d)", tpr);
@@ -117,9 +117,8 @@ int resolve(const tg_sched* in, tg_sched* out) {
         return set_error(TG_EINVAL, "block_size must be a multiple of 32 in [32, 1024] (got %d)", s.block_size);
     if (s.block_size % tpr != 0)
         return set_error(TG_EINVAL, "block_size (%d) not divisible by threads_per_row (%d)", s.block_size, tpr);
-    if (s.split != TG_SPLIT_ROWWISE && s.split != TG_SPLIT_MERGE)
-        return set_error(TG_EINVAL, "split must be TG_SPLIT_ROWWISE, TG_SPLIT_MERGE or TG_SPLIT_AUTO (got %d)",
-                         s.split);
+    if (s.split != TG_SPLIT_ROWWISE && s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_STREAM)
+        return set_error(TG_EINVAL, "split must be TG_SPLIT_ROWWISE, _MERGE, _STREAM or _AUTO (got %d)", s.split);
     if (s.chunk_nnz < 0) return set_error(TG_EINVAL, "chunk_nnz must be >= 0 (got %d)", s.chunk_nnz);
     *out = s;
     return TG_OK;
@@ -324,7 +323,11 @@ int tg_axpy_f64(const double* x, const double* w, double* z, double alpha, doubl
     return axpy_run(x, w, z, alpha, beta, n_eff, sc.block_size, static_cast<cudaStream_t>(stream));
 }
 
-size_t tg_power_workspace_bytes(void) { return power_ws_bytes(); }
+size_t tg_power_workspace_bytes(int64_t nnz, const tg_sched* s) {
+    tg_sched r;
+    if (resolve(s, &r) != TG_OK) return 0;
+    return power_ws_bytes(nnz, r);
+}
 
 int tg_power_step_f64(const tg_csr* A, const double* x, int32_t nparts, int64_t stride, double* y,
                       const tg_sched* s, void* workspace, size_t workspace_bytes, tg_stream_t stream) {

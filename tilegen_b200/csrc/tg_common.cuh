@@ -155,21 +155,39 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Bounded wait on phase `parity` of the mbarrier.  Returns false once 2 s of wall time
 // have passed (the caller records an error and skips the dependent work) instead of
 // spinning forever; every copy this library issues completes in microseconds.
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t a = smem_addr(bar);
+    if (mbar_try(a, parity)) return true;  // fast path: no timer read
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return true;
+        if (mbar_try(a, parity)) return true;
         if (globaltimer_ns() - t0 > 2000000000ull) return false;
     }
+}
+
+// Non-blocking check of phase `parity` (mbarrier.test_wait).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (complete_tx bytes).
@@ -190,6 +208,34 @@ __device__ __forceinline__ T group_sum(T v, unsigned mask) {
     for (int off = W / 2; off > 0; off >>= 1) v += __shfl_xor_sync(mask, v, off, W);
     return v;
 }
+
+// Running sum of products.  fp64 accumulates with fused multiply-adds; fp32 uses
+// compensated (Kahan) summation of the rounded products, so a long fp32 row keeps an
+// error of a few ulps of the row's magnitude instead of growing with its length.  The
+// kernels are HBM-bound, so the three extra adds per term cost no time.
+template <typename T>
+struct Sum;
+
+template <>
+struct Sum<double> {
+    double s = 0.0;
+    __device__ __forceinline__ void mad(double a, double b) { s = fma(a, b, s); }
+    __device__ __forceinline__ void add(double v) { s += v; }
+    __device__ __forceinline__ double get() const { return s; }
+};
+
+template <>
+struct Sum<float> {
+    float s = 0.0f, c = 0.0f;
+    __device__ __forceinline__ void add(float v) {
+        const float y = v - c;
+        const float t = s + y;
+        c = (t - s) - y;
+        s = t;
+    }
+    __device__ __forceinline__ void mad(float a, float b) { add(a * b); }
+    __device__ __forceinline__ float get() const { return s; }
+};
 
 // Epilogue of the SpMV family: plain y = acc, or the fused axpy z = alpha*acc + beta*w.
 template <typename T, bool AXPY>

@@ -54,7 +54,7 @@ DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void*
     d.ktile = is_spmm ? std::min<int64_t>(K, (int64_t)g * vec * d.NCV) : K;
     d.U = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
     d.block = (s.block_size >= 512) ? 512 : (s.block_size >= 256 ? 256 : 128);
-    d.merge = (s.split == TG_SPLIT_MERGE);
+    d.merge = (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM);
     d.S = s.chunk_nnz > 0 ? s.chunk_nnz : 256;
     return d;
 }
@@ -126,7 +126,7 @@ bool dense_dispatch(const DenseChoice& d, bool sp, const DenseArgs<T>& a, cudaSt
 template <typename T>
 size_t dense_ws_bytes(int64_t rows, int64_t nnz, int64_t K, const tg_sched& s, bool is_spmm) {
     (void)rows;
-    if (s.split != TG_SPLIT_MERGE || nnz <= 0 || K <= 0) return 0;
+    if ((s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_STREAM) || nnz <= 0 || K <= 0) return 0;
     // alignment does not change the partial width's upper bound: size for the widest tile
     const DenseChoice d = choose_dense<T>(s, K, is_spmm, nullptr, nullptr);
     const int64_t nchunks = ceil_div(nnz, d.S);

@@ -65,12 +65,12 @@ __device__ __forceinline__ int64_t chunk_first_row(const int64_t* indptr, const 
 // ------------------------------------------------------------------ SpMM
 template <typename T, int G, int VEC, int NCV>
 struct RowAcc {
-    T v[NCV][VEC];
+    Sum<T> v[NCV][VEC];
     __device__ __forceinline__ void zero() {
 #pragma unroll
         for (int m = 0; m < NCV; ++m)
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) v[m][e] = T(0);
+            for (int e = 0; e < VEC; ++e) v[m][e] = Sum<T>();
     }
 };
 
@@ -82,7 +82,7 @@ __device__ __forceinline__ void store_row(T* dst, const RowAcc<T, G, VEC, NCV>& 
         if (col < kt) {
             Vec<T, VEC> r;
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) r.v[e] = acc.v[m][e];
+            for (int e = 0; e < VEC; ++e) r.v[e] = acc.v[m][e].get();
             st_vec<T, VEC>(dst + col, r);
         }
     }
@@ -106,9 +106,10 @@ __device__ __forceinline__ void split_arrive_rows(const DenseArgs<T>& a, int64_t
 #pragma unroll
                 for (int e = 0; e < VEC; ++e) {
                     const int64_t col = col0 + e;
-                    T s = ld_cg(&a.tail[ca * a.kpart + col]);
-                    for (int64_t c = ca + 1; c <= cb; ++c) s += ld_cg(&a.head[c * a.kpart + col]);
-                    if (row < a.row_limit) a.C[row * a.ld + col] = s;
+                    Sum<T> s;
+                    s.add(ld_cg(&a.tail[ca * a.kpart + col]));
+                    for (int64_t c = ca + 1; c <= cb; ++c) s.add(ld_cg(&a.head[c * a.kpart + col]));
+                    if (row < a.row_limit) a.C[row * a.ld + col] = s.get();
                 }
             }
         }
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(512) spmm_kernel(DenseArgs<T> a) {
 #pragma unroll
                     for (int m = 0; m < NCV; ++m)
 #pragma unroll
-                        for (int e = 0; e < VEC; ++e) acc.v[m][e] = fma(cval[u], b[u][m].v[e], acc.v[m][e]);
+                        for (int e = 0; e < VEC; ++e) acc.v[m][e].mad(cval[u], b[u][m].v[e]);
                 }
             }
         }
@@ -263,9 +264,7 @@ __global__ void __launch_bounds__(512) sddmm_kernel(DenseArgs<T> a) {
                     crow[u] = r;
                 }
             }
-            T dot[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) dot[u] = T(0);
+            Sum<T> dot[U];
             for (int64_t kb = 0; kb < a.kt; kb += (int64_t)G * VEC * NCV) {
 #pragma unroll
             for (int u = 0; u < U; ++u) {
@@ -276,14 +275,14 @@ __global__ void __launch_bounds__(512) sddmm_kernel(DenseArgs<T> a) {
                         const Vec<T, VEC> vv = ld_gather_vec<T, VEC>(a.B + cidx[u] * a.ld + col, pg);
                         const Vec<T, VEC> uu = ld_gather_vec<T, VEC>(a.U + crow[u] * a.ld + col, pg);
 #pragma unroll
-                        for (int e = 0; e < VEC; ++e) dot[u] = fma(uu.v[e], vv.v[e], dot[u]);
+                        for (int e = 0; e < VEC; ++e) dot[u].mad(uu.v[e], vv.v[e]);
                     }
                 }
             }
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                T d = group_sum<G>(dot[u], gmask);
+                T d = group_sum<G>(dot[u].get(), gmask);
                 const int64_t q = q0 + u;
                 if (lane == (u % G) && q < ce && crow[u] < a.row_limit) a.C[q] = cval[u] * d;
             }

@@ -187,10 +187,37 @@ bool power_dispatch(int tpr, int u, int v, const PowerArgs& a, int bl, int th, c
 
 }  // namespace
 
-size_t power_ws_bytes() { return power_ws_bytes_impl(); }
+// stream split (tg_stream.cu)
+template <typename T, int MODE>
+int stream_run(const tg_csr& A, const T* x, T* y, const T* w, T alpha, T beta, int nparts, int64_t stride,
+               const tg_sched& s, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t stream_ws_bytes(int64_t nnz, const tg_sched& s, size_t elem);
+
+// Workspace: [norm region: per-CTA partials + ticket | stream plan region].  The two
+// regions are disjoint so the slot reduction of tg_shard_norm2_f64 (run when a new x0
+// is loaded) never touches the partition table a reused stream plan reads.
+static size_t norm_region_bytes() { return (power_ws_bytes_impl() + 255) & ~size_t(255); }
+
+size_t power_ws_bytes(int64_t nnz, const tg_sched& s) {
+    size_t b = norm_region_bytes();
+    if (s.split == TG_SPLIT_STREAM && nnz > 0) b += stream_ws_bytes(nnz, s, sizeof(double));
+    return b;
+}
 
 int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride, double* y, const tg_sched& s,
                    void* ws, size_t ws_bytes, cudaStream_t st) {
+    if (nparts < 1 || stride < A.rows + 1)
+        return set_error(TG_EINVAL, "power step: need nparts >= 1 and stride >= rows + 1 (nparts=%d stride=%lld)",
+                         nparts, (long long)stride);
+    if (s.split == TG_SPLIT_STREAM && A.nnz > 0 &&
+        ((reinterpret_cast<uintptr_t>(A.indices) | reinterpret_cast<uintptr_t>(A.data) |
+          reinterpret_cast<uintptr_t>(A.indptr)) & 15u) == 0)
+    {
+        if (ws == nullptr || ws_bytes < norm_region_bytes())
+            return set_error(TG_ENOMEM, "power step: workspace smaller than its norm region");
+        return stream_run<double, 2>(A, x, y, nullptr, 0.0, 0.0, nparts, stride, s,
+                                     static_cast<char*>(ws) + norm_region_bytes(), ws_bytes - norm_region_bytes(), st);
+    }
     if (ws == nullptr || ws_bytes < power_ws_bytes_impl())
         return set_error(TG_ENOMEM, "power step needs %zu workspace bytes, got %zu", power_ws_bytes_impl(), ws_bytes);
     if (nparts < 1 || stride < A.rows + 1)

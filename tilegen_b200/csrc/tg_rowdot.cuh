@@ -28,7 +28,7 @@ template <typename T, int TPR, int U, int V>
 __device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* __restrict__ val,
                                      const T* __restrict__ x, int64_t p, int64_t pe, int lane, uint64_t ps,
                                      uint64_t pg) {
-    T acc = T(0);
+    Sum<T> acc;
     if constexpr (V == 1) {
         int64_t q = p + lane;
         for (; q + (int64_t)(U - 1) * TPR < pe; q += (int64_t)TPR * U) {
@@ -40,15 +40,15 @@ __device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* _
                 v[u] = ld_stream(val + q + u * TPR, ps);
             }
 #pragma unroll
-            for (int u = 0; u < U; ++u) acc = fma(v[u], ld_gather(x + c[u], pg), acc);
+            for (int u = 0; u < U; ++u) acc.mad(v[u], ld_gather(x + c[u], pg));
         }
-        for (; q < pe; q += TPR) acc = fma(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg), acc);
+        for (; q < pe; q += TPR) acc.mad(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg));
     } else {
         // peel to a V-element boundary, full vectors, then the ragged tail
         int64_t pa = (p + V - 1) / V * V;
         if (pa > pe) pa = pe;
         for (int64_t q = p + lane; q < pa; q += TPR)
-            acc = fma(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg), acc);
+            acc.mad(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg));
         const int64_t nv = (pe - pa) / V;
         int64_t k = lane;
         for (; k + (int64_t)(U - 1) * TPR < nv; k += (int64_t)TPR * U) {
@@ -62,7 +62,7 @@ __device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* _
 #pragma unroll
             for (int u = 0; u < U; ++u)
 #pragma unroll
-                for (int e = 0; e < V; ++e) acc = fma(v[u][e], ld_gather(x + c[u][e], pg), acc);
+                for (int e = 0; e < V; ++e) acc.mad(v[u][e], ld_gather(x + c[u][e], pg));
         }
         for (; k < nv; k += TPR) {
             int64_t c[V];
@@ -70,12 +70,12 @@ __device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* _
             const int64_t q = pa + k * V;
             ld_stream_vec<T, V>(idx + q, val + q, ps, c, v);
 #pragma unroll
-            for (int e = 0; e < V; ++e) acc = fma(v[e], ld_gather(x + c[e], pg), acc);
+            for (int e = 0; e < V; ++e) acc.mad(v[e], ld_gather(x + c[e], pg));
         }
         for (int64_t q = pa + nv * V + lane; q < pe; q += TPR)
-            acc = fma(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg), acc);
+            acc.mad(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg));
     }
-    return acc;
+    return acc.get();
 }
 
 }  // namespace tg

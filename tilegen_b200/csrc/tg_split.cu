@@ -16,7 +16,8 @@ __global__ void partition_kernel(const int64_t* __restrict__ indptr, int64_t row
         if (c1 > nchunks - 1) c1 = nchunks - 1;
         for (int64_t c = c0; c <= c1; ++c) own_first[c] = r;
     }
-    for (int64_t c = tid; c < nchunks; c += stride) cnt[c] = 0;
+    if (cnt)
+        for (int64_t c = tid; c < nchunks; c += stride) cnt[c] = 0;
     if (tid == 0) {
         own_first[nchunks] = rows;
         if (err) *err = 0u;

@@ -72,9 +72,10 @@ __device__ __forceinline__ void split_arrive_scalar(int64_t row, int64_t ca, int
     const int old = atomicAdd(&cnt[ca], 1);
     if (old == (int)(cb - ca)) {
         __threadfence();
-        T s = ld_cg(&tail[ca]);
-        for (int64_t c = ca + 1; c <= cb; ++c) s += ld_cg(&head[c]);
-        if (row < row_limit) y[row] = epi(s, row);
+        Sum<T> s;
+        s.add(ld_cg(&tail[ca]));
+        for (int64_t c = ca + 1; c <= cb; ++c) s.add(ld_cg(&head[c]));
+        if (row < row_limit) y[row] = epi(s.get(), row);
         cnt[ca] = 0;
     }
 }

@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(B) spmv_merge_kernel(SpmvArgs<T> a, Epi<T, AXP
         int64_t j = (lo < n_off && off[lo] == qa) ? lo : lo - 1;
         const bool head = off[j] < qa;
         bool first = true;
-        T acc = T(0);
+        Sum<T> acc;
         int64_t nxt = off[j + 1];
 #pragma unroll
         for (int k = 0; k < I; ++k) {
@@ -166,34 +166,34 @@ __global__ void __launch_bounds__(B) spmv_merge_kernel(SpmvArgs<T> a, Epi<T, AXP
                     const int64_t r = r_lo + j;
                     if (first && head) {
                         h_row = r;
-                        h_val = acc;
+                        h_val = acc.get();
                     } else if (r < a.row_limit) {
-                        a.y[r] = epi(acc, r);
+                        a.y[r] = epi(acc.get(), r);
                     }
                     first = false;
-                    acc = T(0);
+                    acc = Sum<T>();
                     ++j;
                     nxt = off[j + 1];
                 }
-                acc += prod[k];
+                acc.add(prod[k]);
             }
         }
         const int64_t r = r_lo + j;
         if (nxt == qb) {
             if (first && head) {
                 h_row = r;
-                h_val = acc;
+                h_val = acc.get();
             } else if (r < a.row_limit) {
-                a.y[r] = epi(acc, r);
+                a.y[r] = epi(acc.get(), r);
             }
             if (qb == a.nnz)  // trailing empty rows (start == end == nnz)
                 for (int64_t rr = r + 1; rr < a.rows && rr < a.row_limit; ++rr) a.y[rr] = epi(T(0), rr);
         } else if (first && head) {
             h_row = r;  // the whole range lies inside one row that started earlier
-            h_val = acc;
+            h_val = acc.get();
         } else {
             t_row = r;
-            t_val = acc;
+            t_val = acc.get();
         }
     }
 
@@ -209,29 +209,31 @@ __global__ void __launch_bounds__(B) spmv_merge_kernel(SpmvArgs<T> a, Epi<T, AXP
     s_tval[tid] = t_val;
     __syncthreads();
     if (t_row >= 0) {
-        T sum = t_val;
+        Sum<T> sum;
+        sum.add(t_val);
         int u = tid + 1;
         while (u < B && s_hrow[u] == t_row) {
-            sum += s_hval[u];
+            sum.add(s_hval[u]);
             ++u;
         }
         const int64_t row_end = off[t_row - r_lo + 1];
         if (row_end <= ce) {
-            if (t_row < a.row_limit) a.y[t_row] = epi(sum, t_row);
+            if (t_row < a.row_limit) a.y[t_row] = epi(sum.get(), t_row);
         } else {
-            a.tail[c] = sum;
+            a.tail[c] = sum.get();
             split_arrive_scalar(t_row, c, (row_end - 1) / S, a.cnt, a.head, a.tail, a.y, epi, a.row_limit);
         }
     }
     if (tid == 0 && s_hrow[0] >= 0) {
         const int64_t H = s_hrow[0];
-        T sum = s_hval[0];
+        Sum<T> sum;
+        sum.add(s_hval[0]);
         int u = 1;
         while (u < B && s_hrow[u] == H) {
-            sum += s_hval[u];
+            sum.add(s_hval[u]);
             ++u;
         }
-        a.head[c] = sum;
+        a.head[c] = sum.get();
         const int64_t jh = H - r_lo;
         split_arrive_scalar(H, off[jh] / S, (off[jh + 1] - 1) / S, a.cnt, a.head, a.tail, a.y, epi, a.row_limit);
     }
@@ -302,8 +304,23 @@ int64_t merge_chunk_nnz(int block) { return (int64_t)block * kMergeI; }
 
 int merge_block(const tg_sched& s) { return s.block_size == 128 ? 128 : 256; }
 
+// stream split (tg_stream.cu)
+enum StreamModeFwd { kStreamPlain = 0, kStreamAxpy = 1 };
+template <typename T, int MODE>
+int stream_run(const tg_csr& A, const T* x, T* y, const T* w, T alpha, T beta, int nparts, int64_t stride,
+               const tg_sched& s, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t stream_ws_bytes(int64_t nnz, const tg_sched& s, size_t elem);
+
+static bool stream_ok(const tg_csr& A) {
+    return A.nnz > 0 && ((reinterpret_cast<uintptr_t>(A.indices) | reinterpret_cast<uintptr_t>(A.data) |
+                          reinterpret_cast<uintptr_t>(A.indptr)) & 15u) == 0;
+}
+
 size_t spmv_ws_bytes(int64_t rows, int64_t nnz, const tg_sched& s, size_t elem) {
     (void)rows;
+    if (s.split == TG_SPLIT_STREAM && nnz > 0)
+        return std::max(stream_ws_bytes(nnz, s, elem),
+                        split_ws_bytes(ceil_div(nnz, merge_chunk_nnz(merge_block(s))), 1, elem));
     if (s.split != TG_SPLIT_MERGE || nnz <= 0) return 0;
     const int64_t S = merge_chunk_nnz(merge_block(s));
     return split_ws_bytes(ceil_div(nnz, S), 1, elem);
@@ -328,7 +345,15 @@ int spmv_run(const tg_csr& A, const T* x, T* y, const Epi<T, AXPY>& epi, const t
         fill_rows_kernel<T, AXPY><<<(unsigned)blocks, 256, 0, st>>>(y, A.rows, row_limit, epi);
         return check_launch("fill_rows_kernel");
     }
-    if (s.split == TG_SPLIT_MERGE) {
+    if (s.split == TG_SPLIT_STREAM && stream_ok(A)) {
+        if constexpr (AXPY) {
+            return stream_run<T, kStreamAxpy>(A, x, y, epi.w, epi.alpha, epi.beta, 1, 0, s, ws, ws_bytes, st);
+        } else {
+            return stream_run<T, kStreamPlain>(A, x, y, nullptr, T(0), T(0), 1, 0, s, ws, ws_bytes, st);
+        }
+    }
+    if (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM) {
+        // stream needs 16-byte aligned operands; the merge split handles any alignment
         const int B = merge_block(s);
         const int64_t S = merge_chunk_nnz(B);
         const int64_t nchunks = ceil_div(A.nnz, S);

@@ -27,9 +27,11 @@ TG_EBOUNDS = -6
 TG_SPLIT_ROWWISE = 0
 TG_SPLIT_MERGE = 1
 TG_SPLIT_AUTO = 2
+TG_SPLIT_STREAM = 3
 
 TG_FLAG_BOUNDS_CHECK = 1
 TG_FLAG_INJECT_BUG = 2
+TG_FLAG_REUSE_PLAN = 4
 
 STATUS_NAMES = {
     TG_OK: "TG_OK",
@@ -108,7 +110,7 @@ SIGNATURES = {
     "tg_sddmm_f32": (ctypes.c_int, [_CP, _P, _P, _P, _I64, _SP, _P, _SZ, _P]),
     "tg_sddmm_f64": (ctypes.c_int, [_CP, _P, _P, _P, _I64, _SP, _P, _SZ, _P]),
     "tg_axpy_f64": (ctypes.c_int, [_P, _P, _P, _F64, _F64, _I64, _SP, _P]),
-    "tg_power_workspace_bytes": (_SZ, []),
+    "tg_power_workspace_bytes": (_SZ, [_I64, _SP]),
     "tg_power_step_f64": (ctypes.c_int, [_CP, _P, ctypes.c_int32, _I64, _P, _SP, _P, _SZ, _P]),
     "tg_shard_norm2_f64": (ctypes.c_int, [_P, _I64, _I64, _P, _SZ, _P]),
     "tg_power_finalize_f64": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P]),

@@ -112,10 +112,12 @@ class PowerIteration:
 
             self._lib = _lib
             L = _lib.load()
-            self.ws = torch.zeros(int(L.tg_power_workspace_bytes()), dtype=torch.uint8, device=self.device)
+            self._sched_c = sched if sched is not None else self._default_sched()
+            self.ws = torch.zeros(int(L.tg_power_workspace_bytes(self.nnz, ctypes.byref(self._sched_c))),
+                                  dtype=torch.uint8, device=self.device)
             self._desc = _lib.TgCsr(self.rows, n, self.nnz, self.indptr.data_ptr(), self.indices.data_ptr(),
                                     self.data.data_ptr())
-            self._sched_c = sched if sched is not None else self._default_sched()
+            self._planned = False
 
     # -- shard views -------------------------------------------------------------------
     def shard(self, buf) -> "object":
@@ -125,7 +127,8 @@ class PowerIteration:
     # -- GPU implementations -----------------------------------------------------------
     def _default_sched(self):
         s = self._lib.default_schedule()
-        s.threads_per_row, s.unroll, s.vector_width, s.block_size, s.tile = 8, 2, 2, 256, 32
+        s.threads_per_row, s.unroll, s.vector_width, s.block_size, s.tile = 4, 2, 2, 256, 32
+        s.split = self._lib.TG_SPLIT_STREAM
         return s
 
     def _stream(self) -> int:
@@ -133,10 +136,15 @@ class PowerIteration:
 
     def _gpu_step(self, x_full, y_shard) -> None:
         L = self._lib.load()
+        s = self._sched_c
+        if self._planned:  # the partition of this matrix is already in the workspace
+            s = self._lib.TgSched(*[getattr(s, f) for f, _ in s._fields_])
+            s.flags |= self._lib.TG_FLAG_REUSE_PLAN
         self._lib.check(L.tg_power_step_f64(ctypes.byref(self._desc), x_full.data_ptr(), self.parts, self.stride,
-                                            y_shard.data_ptr(), ctypes.byref(self._sched_c), self.ws.data_ptr(),
+                                            y_shard.data_ptr(), ctypes.byref(s), self.ws.data_ptr(),
                                             self.ws.numel(), self._stream()), "tg_power_step_f64")
-        self.kernel_launches += 1
+        self.kernel_launches += 1 if self._planned or self._sched_c.split != self._lib.TG_SPLIT_STREAM else 3
+        self._planned = True
 
     def _gpu_norm2(self, shard) -> None:
         L = self._lib.load()

@@ -162,21 +162,27 @@ def run_launcher(kernel_name: str, A: CSR, data, K: int = 8, sched: "_lib.TgSche
     ix = torch.as_tensor(A.indices).to(dev)
     dv = T(A.data)
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    # every device buffer is bound to a name until the synchronous call returns
     if kernel_name == "spmv":
+        dx = T(x)
         out = torch.zeros(M, dtype=torch.float64, device=dev)
-        L.launch_spmv(p(ip), p(ix), p(dv), p(T(x)), p(out), M, N, nnz)
+        L.launch_spmv(p(ip), p(ix), p(dv), p(dx), p(out), M, N, nnz)
     elif kernel_name == "spmm":
+        dB = T(B)
         out = torch.zeros((M, K), dtype=torch.float64, device=dev)
-        L.launch_spmm(p(ip), p(ix), p(dv), p(T(B)), p(out), M, N, K, nnz)
+        L.launch_spmm(p(ip), p(ix), p(dv), p(dB), p(out), M, N, K, nnz)
     elif kernel_name == "sddmm":
+        dU, dV = T(U), T(V)
         out = torch.zeros(nnz, dtype=torch.float64, device=dev)
-        L.launch_sddmm(p(ip), p(ix), p(dv), p(T(U)), p(T(V)), p(out), M, N, K, nnz)
+        L.launch_sddmm(p(ip), p(ix), p(dv), p(dU), p(dV), p(out), M, N, K, nnz)
     elif kernel_name == "fused_spmv_axpy":
+        dx, dw = T(x), T(w)
         out = torch.zeros(M, dtype=torch.float64, device=dev)
-        L.launch_fused_spmv_axpy(p(ip), p(ix), p(dv), p(T(x)), p(T(w)), p(out), alpha, beta, M, N, nnz)
+        L.launch_fused_spmv_axpy(p(ip), p(ix), p(dv), p(dx), p(dw), p(out), alpha, beta, M, N, nnz)
     elif kernel_name == "axpy":
+        dx, dw = T(x), T(w)
         out = torch.zeros(M, dtype=torch.float64, device=dev)
-        L.launch_axpy(p(T(x)), p(T(w)), p(out), alpha, beta, M)
+        L.launch_axpy(p(dx), p(dw), p(out), alpha, beta, M)
     else:
         raise ValueError("unknown kernel %r" % kernel_name)
     status = L.tg_last_status()
