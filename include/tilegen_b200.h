@@ -172,6 +172,21 @@ TG_API int tg_power_finalize_f64(const double* x, int32_t nparts, int64_t stride
                                  int64_t rows, double* x_out, double* lambda_out,
                                  tg_stream_t stream);
 
+/* ----------------------------------------------- SpMV that allocates nothing */
+/* No counterpart in the reference.  y = A x (fp64, merge split) for callers that can
+ * pass only inputs and outputs -- a host that owns the whole GPU memory pool, or a path
+ * that cannot afford cudaMalloc's implicit synchronisation.  Its scratch is a fixed
+ * 1 MiB array in the library's device memory (on every GPU that loads the library,
+ * until the process exits), so there is no workspace argument and nothing is allocated.
+ * Limit: the partition of A's nonzeros must fit the array -- about 67 million nonzeros
+ * with block_size 256, 33 million with 128; larger calls return TG_EINVAL naming the
+ * limit.  The first call on a device looks up the array's address (cudaGetSymbolAddress)
+ * and should come before any stream capture there.  All calls share the array, so calls
+ * that overlap on the GPU race: order them on one stream.  Bounds checking and plan
+ * reuse are not available here. */
+TG_API int tg_spmv_f64_noalloc(const tg_csr* A, const double* x, double* y, const tg_sched* s,
+                               tg_stream_t stream);
+
 /* --------------------------------------------- reference-compatible launchers */
 /* Signatures as emitted by tilegen/codegen.py:_abi (226-280) for the standard kernels
  * of tilegen/dsl.py:214-256; argument order/meaning as in tilegen/verify.py:166-173. */

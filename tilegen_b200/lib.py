@@ -114,6 +114,7 @@ SIGNATURES = {
     "tg_power_step_f64": (ctypes.c_int, [_CP, _P, ctypes.c_int32, _I64, _P, _SP, _P, _SZ, _P]),
     "tg_shard_norm2_f64": (ctypes.c_int, [_P, _I64, _I64, _P, _SZ, _P]),
     "tg_power_finalize_f64": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P]),
+    "tg_spmv_f64_noalloc": (ctypes.c_int, [_CP, _P, _P, _SP, _P]),
     "launch_spmv": (None, [_P, _P, _P, _P, _P, _I64, _I64, _I64]),
     "launch_spmm": (None, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64]),
     "launch_sddmm": (None, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64]),
