@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--iters", type=int, default=ITERS)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--split", choices=["stream", "rowwise"], default="rowwise")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: fused SpMV + peer-memory push (p2p) or NCCL all-gather")
     ap.add_argument("--tpr", type=int, default=4)
     ap.add_argument("--unroll", type=int, default=2)
     ap.add_argument("--vec", type=int, default=2)
@@ -230,11 +232,13 @@ def run_reference(args, rank: int, world: int):
     return 0
 
 
-def workload_config(n: int, world: int):
+def workload_config(n: int, world: int, exchange: str = "p2p"):
     return {"workload": "C4 power iteration: %dx%d CSR, %d distinct cols/row, fp64, %d iterations/step"
                         % (n, n, C4_PER_ROW, ITERS),
             "rows": n, "nnz": n * C4_PER_ROW, "iterations_per_step": ITERS,
-            "parallelism": "row-sharded x%d, x replicated (in-place NCCL all-gather of shards)" % world,
+            "parallelism": "row-sharded x%d, x replicated (%s)" % (
+                world, "fused SpMV + peer-memory push of shards" if exchange == "p2p" else
+                "in-place NCCL all-gather of shards"),
             "l2": "inputs (%.2f GB) larger than L2 (126 MB): no flush" % (spmv_bytes(n, n, n * C4_PER_ROW) / 1e9)}
 
 
@@ -290,6 +294,8 @@ def main():
     d_d = h_d.to(dev)
     d_x0 = h_x0.to(dev)
     pi = PowerIteration(d_ip, d_ix, d_d, bounds, rank, sched=s)
+    if world > 1 and args.exchange == "p2p":
+        pi.p2p_connect()
     del d_ix
     x_out = torch.empty(r1 - r0, dtype=torch.float64, device=dev)
     lam = torch.empty(1, dtype=torch.float64, device=dev)
@@ -349,6 +355,8 @@ def main():
         dd = h_d.to(dev, non_blocking=True)
         xx = h_x0.to(dev, non_blocking=True)
         pe = PowerIteration(ip, ix, dd, bounds, rank, sched=s)
+        if world > 1 and args.exchange == "p2p":
+            pe.p2p_connect()
         del ix
         pe.set_x0(xx)
         pe.iterate(args.iters)
@@ -376,7 +384,8 @@ def main():
         peak, peak_kind = measured_peaks()
         local_bytes = spmv_bytes(r1 - r0, n, shard.nnz)
         achieved = local_bytes / (k_ms / 1e3) / 1e9
-        kname = "spmv_stream_kernel(power)" if args.split == "stream" else "power_step_kernel"
+        kname = "spmv_stream_kernel(power)" if args.split == "stream" else (
+            "power_p2p_kernel" if (world > 1 and args.exchange == "p2p") else "power_step_kernel")
         tr = traffic_record("c4_%d" % world, kname)
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(achieved / peak, 4), "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"
@@ -397,7 +406,7 @@ def main():
             "vs_baseline": None,
             "dtype": "f64",
             "data": "synthetic (seeded C4 generator, values U(-1,1))",
-            "config": workload_config(n, world),
+            "config": workload_config(n, world, args.exchange),
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(h_ip.numel() * 8 + h_ix.numel() * 8 + h_d.numel() * 8 + h_x0.numel() * 8),
                     "d2h_bytes_per_step": int(h_xout.numel() * 8 + 8), "ms_per_step": round(e2e_step_ms, 3)},

@@ -172,6 +172,37 @@ TG_API int tg_power_finalize_f64(const double* x, int32_t nparts, int64_t stride
                                  int64_t rows, double* x_out, double* lambda_out,
                                  tg_stream_t stream);
 
+/* Power step fused with the shard exchange over peer memory (1..8 GPUs of one node).
+ * y_peers[q] is rank q's next-iterate buffer (nparts * stride doubles) and flag_peers[q]
+ * rank q's flag array (nparts uint64, zero-filled before the first epoch), both mapped
+ * into this process (CUDA IPC); index `rank` is this rank's own.  The kernel waits
+ * (bounded, 2 s) until flag_peers[rank][q] >= epoch-1 for every q, computes its shard
+ * tile by tile and stores each tile into every y_peers[q], writes its slot to all
+ * ranks, then stores `epoch` into flag_peers[q][rank] (system-scope release).  Call with
+ * epoch = 1, 2, ... and alternate two iterate buffers.  A wait that runs out sets bit 4
+ * (value 16) of the workspace's error word (read it with tg_power_error) and skips the
+ * step.  Plain peer stores only: no multicast, no TMA. */
+TG_API int tg_power_step_p2p_f64(const tg_csr* A, const double* x, int32_t nparts, int32_t rank,
+                                 int64_t stride, double* const* y_peers, uint64_t* const* flag_peers,
+                                 uint64_t epoch, const tg_sched* s, void* workspace,
+                                 size_t workspace_bytes, tg_stream_t stream);
+/* Copies the power workspace's error word to *err (synchronises `stream`): 16 = a peer
+ * wait ran out.  Zero when nothing went wrong. */
+TG_API int tg_power_error(const void* workspace, uint32_t* err, tg_stream_t stream);
+/* Bounded wait (2 s) until every entry of this rank's flag array reached `epoch`: the
+ * pushes of the last step have landed and the local iterate is complete. */
+TG_API int tg_p2p_wait(const uint64_t* flag_local, int32_t nparts, uint64_t epoch, void* workspace,
+                       size_t workspace_bytes, tg_stream_t stream);
+
+/* Exchange buffers of the fused step: device memory from cudaMalloc (zero-filled), so
+ * that a CUDA IPC handle maps the buffer itself.  tg_ipc_open maps a peer's buffer into
+ * the current device's context with lazy peer access; close it before the owner frees. */
+TG_API int tg_peer_buffer_alloc(size_t bytes, void** ptr);
+TG_API int tg_peer_buffer_free(void* ptr);
+TG_API int tg_ipc_get_handle(const void* ptr, void* handle /* 64 bytes */);
+TG_API int tg_ipc_open(const void* handle /* 64 bytes */, void** ptr);
+TG_API int tg_ipc_close(void* ptr);
+
 /* ----------------------------------------------- SpMV that allocates nothing */
 /* No counterpart in the reference.  y = A x (fp64, merge split) for callers that can
  * pass only inputs and outputs -- a host that owns the whole GPU memory pool, or a path

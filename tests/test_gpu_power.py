@@ -101,3 +101,51 @@ def test_power_step_is_deterministic(split):
         pi.iterate(5)
         outs.append(pi.x[pi.cur].cpu().numpy())
     assert np.array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("parts", [2, 3, 8])
+def test_p2p_fused_step_emulated_on_one_gpu(parts):
+    """tg_power_step_p2p_f64 with every rank's buffers on one device: per epoch the
+    ranks' kernels run one after another on one stream, so each wait is already met when
+    its kernel starts (nothing waits on a kernel that has not run).  Checks the pushes
+    into every rank's next iterate, the slot broadcast and the epoch flags."""
+    A = M.baseline_matrix("c3", scale=0.3)
+    n = A.rows
+    bounds = nnz_balanced_bounds(A.row_lengths(), parts)
+    dev = torch.device("cuda")
+    pis = []
+    for r in range(parts):
+        a, b = int(bounds[r]), int(bounds[r + 1])
+        ip = A.indptr[a:b + 1] - A.indptr[a]
+        sl = slice(int(A.indptr[a]), int(A.indptr[b]))
+        pis.append(PowerIteration(torch.as_tensor(ip).to(dev), torch.as_tensor(A.indices[sl]).to(dev),
+                                  torch.as_tensor(A.data[sl]).to(dev), bounds, r, sched=_sched(4, 2, 2),
+                                  exchange=lambda x: None))
+    flags = [torch.zeros(parts, dtype=torch.int64, device=dev) for _ in range(parts)]
+    for pi in pis:
+        pi.p2p_setup([(q.x[0], q.x[1]) for q in pis], flags)
+    stride = pis[0].stride
+    x0 = np.random.default_rng(2).uniform(-1, 1, n)
+    for r, pi in enumerate(pis):
+        pi.set_x0(torch.as_tensor(x0[bounds[r]:bounds[r + 1]]).to(dev))
+    for r in range(parts):  # emulated all-gather of the initial shards
+        src = pis[r].x[0][r * stride:(r + 1) * stride]
+        for q in range(parts):
+            if q != r:
+                pis[q].x[0][r * stride:(r + 1) * stride].copy_(src)
+    cur = 0
+    iters = 9
+    for _ in range(iters):
+        for pi in pis:
+            pi.p2p_step(cur)
+        cur = 1 - cur
+    for pi in pis:
+        pi.cur = cur
+        pi.p2p_wait()
+    torch.cuda.synchronize()
+    assert all(int(f.min()) == iters for f in flags)
+    assert all(pi.error_word() == 0 for pi in pis)
+    x = np.concatenate([pi.result()[0].cpu().numpy() for pi in pis])
+    xr, nr = O.power_iteration(A, x0, iters)
+    assert rel(x, xr) <= 1e-9
+    assert abs(float(pis[0].result()[1]) - nr) <= 1e-9 * nr

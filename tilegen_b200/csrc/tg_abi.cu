@@ -50,6 +50,12 @@ int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride,
 int shard_norm2_run(double* shard, int64_t rows, int64_t stride, void* ws, size_t ws_bytes, cudaStream_t st);
 int power_finalize_run(const double* x, int nparts, int64_t stride, int part, int64_t rows, double* x_out,
                        double* lambda_out, cudaStream_t st);
+int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, int64_t stride,
+                       double* const* y_peers, unsigned long long* const* flag_peers, unsigned long long epoch,
+                       const tg_sched& s, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t power_err_offset();
+int p2p_wait_run(const unsigned long long* flag_local, int nparts, unsigned long long epoch, void* ws,
+                 size_t ws_bytes, cudaStream_t st);
 
 // ------------------------------------------------------------------ bounds check
 // Sets bits of *err: 1 indptr[0] != 0, 2 indptr decreasing, 4 indptr[rows] != nnz,
@@ -350,6 +356,66 @@ int tg_power_finalize_f64(const double* x, int32_t nparts, int64_t stride, int32
         return set_error(TG_EINVAL, "tg_power_finalize_f64: bad arguments");
     return power_finalize_run(x, nparts, stride, part, rows, x_out, lambda_out, static_cast<cudaStream_t>(stream));
 }
+
+int tg_power_step_p2p_f64(const tg_csr* A, const double* x, int32_t nparts, int32_t rank, int64_t stride,
+                          double* const* y_peers, uint64_t* const* flag_peers, uint64_t epoch, const tg_sched* s,
+                          void* workspace, size_t workspace_bytes, tg_stream_t stream) {
+    TG_PRELUDE("tg_power_step_p2p_f64");
+    if (!x || !y_peers || !flag_peers) return set_error(TG_EINVAL, "tg_power_step_p2p_f64: null pointer");
+    return power_step_p2p_run(*A, x, nparts, rank, stride, y_peers,
+                              reinterpret_cast<unsigned long long* const*>(flag_peers), epoch, sc, workspace,
+                              workspace_bytes, st);
+}
+
+int tg_power_error(const void* workspace, uint32_t* err, tg_stream_t stream) {
+    if (!workspace || !err) return set_error(TG_EINVAL, "tg_power_error: null argument");
+    const char* w = static_cast<const char*>(workspace) + power_err_offset();
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc = check_cuda(cudaMemcpyAsync(err, w, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync");
+    if (rc != TG_OK) return rc;
+    return check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+}
+
+int tg_p2p_wait(const uint64_t* flag_local, int32_t nparts, uint64_t epoch, void* workspace, size_t workspace_bytes,
+                tg_stream_t stream) {
+    return p2p_wait_run(reinterpret_cast<const unsigned long long*>(flag_local), nparts, epoch, workspace,
+                        workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------ peer buffers (multi-GPU exchange)
+int tg_peer_buffer_alloc(size_t bytes, void** ptr) {
+    if (!ptr || bytes == 0) return set_error(TG_EINVAL, "tg_peer_buffer_alloc: bad arguments");
+    *ptr = nullptr;
+    int rc = check_cuda(cudaMalloc(ptr, bytes), "cudaMalloc(peer buffer)");
+    if (rc != TG_OK) return rc;
+    rc = check_cuda(cudaMemset(*ptr, 0, bytes), "cudaMemset(peer buffer)");
+    if (rc != TG_OK) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+    }
+    return rc;
+}
+
+int tg_peer_buffer_free(void* ptr) { return ptr ? check_cuda(cudaFree(ptr), "cudaFree(peer buffer)") : TG_OK; }
+
+int tg_ipc_get_handle(const void* ptr, void* handle) {
+    if (!ptr || !handle) return set_error(TG_EINVAL, "tg_ipc_get_handle: null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    int rc = check_cuda(cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)), "cudaIpcGetMemHandle");
+    if (rc == TG_OK) memcpy(handle, &h, sizeof(h));
+    return rc;
+}
+
+int tg_ipc_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return set_error(TG_EINVAL, "tg_ipc_open: null argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *ptr = nullptr;
+    return check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int tg_ipc_close(void* ptr) { return ptr ? check_cuda(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle") : TG_OK; }
 
 // ------------------------------------------------ reference-compatible launchers
 static void finish_shim(int rc) {

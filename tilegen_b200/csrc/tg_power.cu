@@ -109,6 +109,141 @@ __global__ void __launch_bounds__(1024) power_step_kernel(PowerArgs a) {
     grid_sum_last(part, a.partials, a.ticket, a.y + a.stride - 1);
 }
 
+// ------------------------------------------------------------------ fused exchange
+// The power step fused with the shard exchange over peer memory (1..8 GPUs, CUDA IPC
+// mappings, plain P2P stores, no multicast).  Iteration `epoch` reads the local copy of
+// the iterate x (all shards) and writes its own shard of the next iterate straight into
+// every rank's next-iterate buffer y_peers[q] (own rank included), one tile of rows at a
+// time, so the NVLink transfer overlaps the SpMV.  Protocol, per kernel:
+//   1. wait (bounded, 2 s) until every rank's flag in the LOCAL flag array reached
+//      epoch-1: all ranks finished the previous iteration, so the local x is complete
+//      and nobody still reads the buffer this kernel writes;
+//   2. rowwise SpMV of the tile, y = s * (A x) staged in shared memory, pushed to every
+//      rank with coalesced 8-byte stores;
+//   3. each CTA fences (system scope) and takes a ticket; the last CTA sums the norm
+//      partials in CTA order, writes the slot to every rank, fences, and release-stores
+//      `epoch` into flag_peers[q][rank] for every q.
+// A wait that runs out sets bit 4 of *err and skips the step; the host reads *err.
+struct PowerP2PArgs {
+    const int64_t* indptr;
+    const int64_t* indices;
+    const double* data;
+    const double* x;  // local padded iterate (nparts * stride)
+    int nparts;
+    int rank;
+    int64_t stride;
+    double* y_peers[8];          // next-iterate buffer of every rank (nparts * stride each)
+    unsigned long long* flag_peers[8];  // flag array (nparts words) of every rank
+    unsigned long long* flag_local;     // this rank's flag array
+    unsigned long long epoch;
+    int64_t rows;
+    double* partials;
+    unsigned* ticket;
+    uint32_t* err;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+template <int TPR, int U, int V>
+__global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
+    constexpr int kGroups = 256 / TPR;  // rows per CTA tile: one per lane group
+    constexpr int kWarpRows = 32 / TPR; // consecutive rows owned by one warp per tile
+    __shared__ double s_warp[32];
+    __shared__ double s_scale;
+    __shared__ int s_ok;
+    const uint64_t ps = policy_evict_first();
+    const uint64_t pg = policy_evict_last();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const uint64_t t0 = globaltimer_ns();
+        for (int q = 0; q < a.nparts && ok; ++q) {
+            while (ld_acquire_sys(&a.flag_local[q]) + 1 < a.epoch) {
+                if (globaltimer_ns() - t0 > 2000000000ull) {
+                    ok = 0;
+                    atomicOr(a.err, 16u);
+                    break;
+                }
+            }
+        }
+        s_ok = ok;
+        double t = 0.0;
+        if (ok)
+            for (int r = 0; r < a.nparts; ++r) t += a.x[(int64_t)r * a.stride + a.stride - 1];
+        s_scale = t > 0.0 ? 1.0 / sqrt(t) : 0.0;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    __threadfence_system();
+    const double scale = s_scale;
+    const int lane = threadIdx.x % TPR;
+    const int group = threadIdx.x / TPR;
+    const int wl = threadIdx.x & 31;
+    unsigned mask = kFull;
+    if constexpr (TPR < 32) mask = ((1u << TPR) - 1u) << ((threadIdx.x % 32) / TPR * TPR);
+    const int64_t own = (int64_t)a.rank * a.stride;
+    double sq = 0.0;
+    for (int64_t base = (int64_t)blockIdx.x * kGroups; base < a.rows; base += (int64_t)gridDim.x * kGroups) {
+        const int64_t i = base + group;
+        double v = 0.0;
+        if (i < a.rows) {
+            double acc = row_dot<double, TPR, U, V>(a.indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
+            if constexpr (TPR > 1) acc = group_sum<TPR>(acc, mask);
+            v = scale * acc;
+            if (lane == 0) sq = fma(v, v, sq);
+        }
+        // the warp's kWarpRows results to lanes 0..kWarpRows-1, then one coalesced
+        // kWarpRows*8-byte segment per rank (lanes spread over the ranks)
+        const int src = (wl % kWarpRows) * TPR;
+        const double mine = __shfl_sync(kFull, v, src);
+        const int64_t row0 = base + (threadIdx.x / 32) * kWarpRows;
+        const int64_t r = row0 + (wl % kWarpRows);
+        if (r < a.rows)
+            for (int q = wl / kWarpRows; q < a.nparts; q += 32 / kWarpRows) a.y_peers[q][own + r] = mine;
+    }
+    const double part = block_sum(sq, s_warp);
+    __shared__ bool s_last;
+    if (threadIdx.x == 0) {
+        a.partials[blockIdx.x] = part;
+        __threadfence_system();
+        s_last = (atomicAdd(a.ticket, 1u) == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (s_last && threadIdx.x < 32) {
+        __threadfence_system();
+        double v = 0.0;
+        for (unsigned i = threadIdx.x; i < gridDim.x; i += 32) v += __ldcg(&a.partials[i]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off);  // every lane: the total
+        if (threadIdx.x < a.nparts) a.y_peers[threadIdx.x][own + a.stride - 1] = v;
+        __threadfence_system();
+        __syncwarp();
+        if (threadIdx.x < a.nparts) st_release_sys(&a.flag_peers[threadIdx.x][a.rank], a.epoch);
+        if (threadIdx.x == 0) *a.ticket = 0u;
+    }
+}
+
+// Bounded wait (2 s) until every rank's flag reached `epoch` (the last iteration's
+// pushes have all landed); bit 4 of *err on timeout.
+__global__ void p2p_wait_kernel(const unsigned long long* flag_local, int nparts, unsigned long long epoch,
+                                uint32_t* err) {
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < nparts; ++q)
+        while (ld_acquire_sys(&flag_local[q]) < epoch)
+            if (globaltimer_ns() - t0 > 2000000000ull) {
+                atomicOr(err, 16u);
+                return;
+            }
+    __threadfence_system();
+}
+
 // slot <- sum(shard[0..rows)^2), same deterministic reduction.
 __global__ void shard_norm2_kernel(double* shard, int64_t rows, int64_t stride, double* partials, unsigned* ticket) {
     __shared__ double s_warp[32];
@@ -142,6 +277,11 @@ struct PowerWs {
 };
 
 size_t power_ws_bytes_impl() { return sizeof(double) * kPowerMaxGrid + 256; }
+
+// error word of the fused-exchange path: inside the norm region, after the ticket
+uint32_t* p2p_err_word(void* ws) {
+    return reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + sizeof(double) * kPowerMaxGrid + 8);
+}
 
 PowerWs carve(void* ws) {
     PowerWs w;
@@ -246,6 +386,66 @@ int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride,
     if (!power_dispatch(tpr, u, v, a, (int)blocks, threads, st))
         return set_error(TG_EUNSUPPORTED, "no power-step instance for TPR=%d U=%d V=%d", tpr, u, v);
     return check_launch("power_step_kernel");
+}
+
+template <int TPR, int U, int V>
+static void launch_p2p(const PowerP2PArgs& a, int blocks, cudaStream_t st) {
+    power_p2p_kernel<TPR, U, V><<<blocks, 256, 0, st>>>(a);
+}
+
+int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, int64_t stride,
+                       double* const* y_peers, unsigned long long* const* flag_peers, unsigned long long epoch,
+                       const tg_sched& s, void* ws, size_t ws_bytes, cudaStream_t st) {
+    if (nparts < 1 || nparts > 8 || rank < 0 || rank >= nparts || stride < A.rows + 1)
+        return set_error(TG_EINVAL, "p2p step: bad nparts/rank/stride (%d, %d, %lld)", nparts, rank, (long long)stride);
+    if (epoch < 1) return set_error(TG_EINVAL, "p2p step: epoch must be >= 1");
+    if (ws == nullptr || ws_bytes < power_ws_bytes_impl())
+        return set_error(TG_ENOMEM, "p2p step needs %zu workspace bytes", power_ws_bytes_impl());
+    PowerWs w = carve(ws);
+    PowerP2PArgs a{};
+    a.indptr = A.indptr;
+    a.indices = A.indices;
+    a.data = static_cast<const double*>(A.data);
+    a.x = x;
+    a.nparts = nparts;
+    a.rank = rank;
+    a.stride = stride;
+    for (int q = 0; q < nparts; ++q) {
+        if (!y_peers[q] || !flag_peers[q]) return set_error(TG_EINVAL, "p2p step: null peer pointer %d", q);
+        a.y_peers[q] = y_peers[q];
+        a.flag_peers[q] = flag_peers[q];
+    }
+    a.flag_local = flag_peers[rank];
+    a.epoch = epoch;
+    a.rows = A.rows;
+    a.partials = w.partials;
+    a.ticket = w.ticket;
+    a.err = p2p_err_word(ws);
+    const int tpr = s.threads_per_row <= 4 ? 4 : 8;
+    const int u = s.unroll >= 2 ? 2 : 1;
+    int v = s.vector_width >= 2 ? 2 : 1;
+    if ((reinterpret_cast<uintptr_t>(A.indices) | reinterpret_cast<uintptr_t>(A.data)) & 15u) v = 1;
+    int64_t blocks = ceil_div(std::max<int64_t>(A.rows, 1), 256 / tpr);
+    blocks = std::min<int64_t>(blocks, kPowerMaxGrid);
+    if (tpr == 4) {
+        if (u == 2) { if (v == 2) launch_p2p<4, 2, 2>(a, (int)blocks, st); else launch_p2p<4, 2, 1>(a, (int)blocks, st); }
+        else { if (v == 2) launch_p2p<4, 1, 2>(a, (int)blocks, st); else launch_p2p<4, 1, 1>(a, (int)blocks, st); }
+    } else {
+        if (u == 2) { if (v == 2) launch_p2p<8, 2, 2>(a, (int)blocks, st); else launch_p2p<8, 2, 1>(a, (int)blocks, st); }
+        else { if (v == 2) launch_p2p<8, 1, 2>(a, (int)blocks, st); else launch_p2p<8, 1, 1>(a, (int)blocks, st); }
+    }
+    return check_launch("power_p2p_kernel");
+}
+
+size_t power_err_offset() { return sizeof(double) * kPowerMaxGrid + 8; }
+
+int p2p_wait_run(const unsigned long long* flag_local, int nparts, unsigned long long epoch, void* ws,
+                 size_t ws_bytes, cudaStream_t st) {
+    if (!flag_local || nparts < 1 || nparts > 8) return set_error(TG_EINVAL, "p2p wait: bad arguments");
+    if (ws == nullptr || ws_bytes < power_ws_bytes_impl())
+        return set_error(TG_ENOMEM, "p2p wait needs %zu workspace bytes", power_ws_bytes_impl());
+    p2p_wait_kernel<<<1, 1, 0, st>>>(flag_local, nparts, epoch, p2p_err_word(ws));
+    return check_launch("p2p_wait_kernel");
 }
 
 int shard_norm2_run(double* shard, int64_t rows, int64_t stride, void* ws, size_t ws_bytes, cudaStream_t st) {

@@ -114,6 +114,15 @@ SIGNATURES = {
     "tg_power_step_f64": (ctypes.c_int, [_CP, _P, ctypes.c_int32, _I64, _P, _SP, _P, _SZ, _P]),
     "tg_shard_norm2_f64": (ctypes.c_int, [_P, _I64, _I64, _P, _SZ, _P]),
     "tg_power_finalize_f64": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P]),
+    "tg_power_step_p2p_f64": (ctypes.c_int, [_CP, _P, ctypes.c_int32, ctypes.c_int32, _I64, _P, _P,
+                                             ctypes.c_uint64, _SP, _P, _SZ, _P]),
+    "tg_p2p_wait": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_uint64, _P, _SZ, _P]),
+    "tg_power_error": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
+    "tg_peer_buffer_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(ctypes.c_void_p)]),
+    "tg_peer_buffer_free": (ctypes.c_int, [_P]),
+    "tg_ipc_get_handle": (ctypes.c_int, [_P, ctypes.c_char_p]),
+    "tg_ipc_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "tg_ipc_close": (ctypes.c_int, [_P]),
     "tg_spmv_f64_noalloc": (ctypes.c_int, [_CP, _P, _P, _SP, _P]),
     "launch_spmv": (None, [_P, _P, _P, _P, _P, _I64, _I64, _I64]),
     "launch_spmm": (None, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64]),

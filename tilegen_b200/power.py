@@ -67,6 +67,31 @@ def renumber_columns(indices, bounds, stride: int):
     return owner * stride + (indices - b[owner])
 
 
+class _PeerPtr:
+    """A device address mapped from another rank (only its data_ptr is used)."""
+
+    def __init__(self, ptr: int):
+        self.ptr = int(ptr)
+
+    def data_ptr(self) -> int:
+        return self.ptr
+
+
+class _CudaArray:
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+def _device_view(ptr: int, n: int, dtype, device):
+    """A torch tensor over n elements of device memory at ptr (no copy, not owning)."""
+    import torch
+
+    typestr = {torch.float64: "<f8", torch.int64: "<i8"}[dtype]
+    with torch.cuda.device(device):
+        return torch.as_tensor(_CudaArray(ptr, n, typestr), device=device)
+
+
 class PowerIteration:
     """One rank of the sharded power iteration.
 
@@ -107,6 +132,8 @@ class PowerIteration:
         self._finalize = finalize or self._gpu_finalize
         self._exchange = exchange or (self._nccl_exchange if self.parts > 1 else (lambda x: None))
         self.kernel_launches = 0
+        self.p2p = False
+        self.epoch = 0
         if step is None or norm2 is None or finalize is None:
             from . import lib as _lib
 
@@ -157,6 +184,109 @@ class PowerIteration:
 
         dist.all_gather_into_tensor(x_full, self.shard(x_full))
 
+    # -- fused exchange over peer memory ------------------------------------------------
+    def p2p_setup(self, peer_x, peer_flags) -> None:
+        """Switch iterate() to the fused step (tg_power_step_p2p_f64).  peer_x[q] is the
+        pair (x[0], x[1]) of rank q and peer_flags[q] its flag array (int64, zeroed),
+        all accessible from this device (local tensors, or peer memory mapped by CUDA
+        IPC); index self.rank must be this object's own x and flags."""
+        if len(peer_x) != self.parts or len(peer_flags) != self.parts:
+            raise ValueError("need one buffer pair and one flag array per rank")
+        P = ctypes.c_void_p * 8
+        self._y_ptrs = [P(*([int(px[b].data_ptr()) for px in peer_x] + [0] * (8 - self.parts))) for b in (0, 1)]
+        self._flag_ptrs = P(*([int(f.data_ptr()) for f in peer_flags] + [0] * (8 - self.parts)))
+        self._flags_local = peer_flags[self.rank]
+        self._peer_keep = (peer_x, peer_flags)
+        self.epoch = 0
+        self.p2p = True
+
+    def p2p_connect(self, group=None) -> None:
+        """Allocate x[0], x[1] and a zeroed flag array as peer-shareable buffers, exchange
+        their CUDA IPC handles with every rank of the process group, map the peers'
+        buffers into this device's context, then p2p_setup.  close() releases them."""
+        import torch.distributed as dist
+
+        torch = self.torch
+        L = self._lib.load()
+        n = self.parts * self.stride
+        self._owned = []
+        mine = []
+        for nbytes in (8 * n, 8 * n, 8 * self.parts):
+            p = ctypes.c_void_p()
+            self._lib.check(L.tg_peer_buffer_alloc(nbytes, ctypes.byref(p)), "tg_peer_buffer_alloc")
+            self._owned.append(p.value)
+            h = ctypes.create_string_buffer(64)
+            self._lib.check(L.tg_ipc_get_handle(p.value, h), "tg_ipc_get_handle")
+            mine.append(h.raw)
+        xa = _device_view(self._owned[0], n, torch.float64, self.device)
+        xb = _device_view(self._owned[1], n, torch.float64, self.device)
+        fl = _device_view(self._owned[2], self.parts, torch.int64, self.device)
+        xa.copy_(self.x[0])
+        xb.copy_(self.x[1])
+        self.x = [xa, xb]
+        allh = [None] * self.parts
+        dist.all_gather_object(allh, mine, group=group)
+        self._opened = []
+        peer_x, peer_flags = [], []
+        for q, hs in enumerate(allh):
+            if q == self.rank:
+                peer_x.append((xa, xb))
+                peer_flags.append(fl)
+                continue
+            ptrs = []
+            for h in hs:
+                p = ctypes.c_void_p()
+                self._lib.check(L.tg_ipc_open(h, ctypes.byref(p)), "tg_ipc_open")
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            peer_x.append((_PeerPtr(ptrs[0]), _PeerPtr(ptrs[1])))
+            peer_flags.append(_PeerPtr(ptrs[2]))
+        self.p2p_setup(peer_x, peer_flags)
+        self._group = group
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then (after every rank did) free this rank's."""
+        if not getattr(self, "_owned", None):
+            return
+        import torch.distributed as dist
+
+        self.torch.cuda.synchronize(self.device)
+        L = self._lib.load()
+        for p in self._opened:
+            L.tg_ipc_close(p)
+        self._opened = []
+        dist.barrier(group=self._group)
+        self.x = [self.x[0].clone(), self.x[1].clone()]
+        self._peer_keep = None
+        for p in self._owned:
+            L.tg_peer_buffer_free(p)
+        self._owned = []
+        self.p2p = False
+
+    def p2p_step(self, src_index: int) -> None:
+        """One fused step: read self.x[src_index], push into every rank's other buffer."""
+        L = self._lib.load()
+        self.epoch += 1
+        self._lib.check(L.tg_power_step_p2p_f64(ctypes.byref(self._desc), self.x[src_index].data_ptr(), self.parts,
+                                                self.rank, self.stride, self._y_ptrs[1 - src_index],
+                                                self._flag_ptrs, self.epoch, ctypes.byref(self._sched_c),
+                                                self.ws.data_ptr(), self.ws.numel(), self._stream()),
+                        "tg_power_step_p2p_f64")
+        self.kernel_launches += 1
+
+    def p2p_wait(self) -> None:
+        L = self._lib.load()
+        self._lib.check(L.tg_p2p_wait(self._flags_local.data_ptr(), self.parts, self.epoch, self.ws.data_ptr(),
+                                      self.ws.numel(), self._stream()), "tg_p2p_wait")
+        self.kernel_launches += 1
+
+    def error_word(self) -> int:
+        L = self._lib.load()
+        v = ctypes.c_uint32(0)
+        self._lib.check(L.tg_power_error(self.ws.data_ptr(), ctypes.byref(v), self._stream()), "tg_power_error")
+        return int(v.value)
+
     # -- iteration ---------------------------------------------------------------------
     def set_x0(self, x0_local) -> None:
         """Start from x0 (this rank's rows); any scale (the first step normalises)."""
@@ -172,11 +302,17 @@ class PowerIteration:
             src, dst = self.x[self.cur], self.x[1 - self.cur]
             if on_step:
                 on_step(2 * k)
-            self._step(src, self.shard(dst))
+            if self.p2p:
+                self.p2p_step(self.cur)
+            else:
+                self._step(src, self.shard(dst))
             if on_step:
                 on_step(2 * k + 1)
-            self._exchange(dst)
+            if not self.p2p:
+                self._exchange(dst)
             self.cur = 1 - self.cur
+        if self.p2p and iters > 0:
+            self.p2p_wait()
 
     def _gpu_finalize(self, x_full, x_out, lam_out) -> None:
         L = self._lib.load()
