@@ -236,9 +236,10 @@ def workload_config(n: int, world: int, exchange: str = "p2p"):
     return {"workload": "C4 power iteration: %dx%d CSR, %d distinct cols/row, fp64, %d iterations/step"
                         % (n, n, C4_PER_ROW, ITERS),
             "rows": n, "nnz": n * C4_PER_ROW, "iterations_per_step": ITERS,
-            "parallelism": "row-sharded x%d, x replicated (%s)" % (
-                world, "fused SpMV + peer-memory push of shards" if exchange == "p2p" else
-                "in-place NCCL all-gather of shards"),
+            "parallelism": ("single GPU, no exchange" if world == 1 else
+                            "row-sharded x%d, x replicated (%s)" % (
+                                world, "fused SpMV + peer-memory push of shards" if exchange == "p2p" else
+                                "in-place NCCL all-gather of shards")),
             "l2": "inputs (%.2f GB) larger than L2 (126 MB): no flush" % (spmv_bytes(n, n, n * C4_PER_ROW) / 1e9)}
 
 
@@ -356,7 +357,7 @@ def main():
         xx = h_x0.to(dev, non_blocking=True)
         pe = PowerIteration(ip, ix, dd, bounds, rank, sched=s)
         if world > 1 and args.exchange == "p2p":
-            pe.p2p_connect()
+            pe.p2p_attach(pi.exchange_state)  # the mappings do not depend on the matrix
         del ix
         pe.set_x0(xx)
         pe.iterate(args.iters)

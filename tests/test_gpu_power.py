@@ -144,6 +144,7 @@ def test_p2p_fused_step_emulated_on_one_gpu(parts):
         pi.p2p_wait()
     torch.cuda.synchronize()
     assert all(int(f.min()) == iters for f in flags)
+    assert all(pi.exchange_state.epoch == iters for pi in pis)
     assert all(pi.error_word() == 0 for pi in pis)
     x = np.concatenate([pi.result()[0].cpu().numpy() for pi in pis])
     xr, nr = O.power_iteration(A, x0, iters)

@@ -67,6 +67,23 @@ def renumber_columns(indices, bounds, stride: int):
     return owner * stride + (indices - b[owner])
 
 
+class _Exchange:
+    """State of the fused exchange: this rank's iterate buffers, the peers' mapped
+    buffers and flag arrays (as pointer arrays for the C ABI), and the epoch counter,
+    which keeps increasing for as long as the flag arrays are in use."""
+
+    def __init__(self):
+        self.y_ptrs = None
+        self.flag_ptrs = None
+        self.flags_local = None
+        self.keep = None
+        self.x = None
+        self.epoch = 0
+        self.owned = []
+        self.opened = []
+        self.group = None
+
+
 class _PeerPtr:
     """A device address mapped from another rank (only its data_ptr is used)."""
 
@@ -133,7 +150,7 @@ class PowerIteration:
         self._exchange = exchange or (self._nccl_exchange if self.parts > 1 else (lambda x: None))
         self.kernel_launches = 0
         self.p2p = False
-        self.epoch = 0
+        self._ex = None
         if step is None or norm2 is None or finalize is None:
             from . import lib as _lib
 
@@ -193,11 +210,20 @@ class PowerIteration:
         if len(peer_x) != self.parts or len(peer_flags) != self.parts:
             raise ValueError("need one buffer pair and one flag array per rank")
         P = ctypes.c_void_p * 8
-        self._y_ptrs = [P(*([int(px[b].data_ptr()) for px in peer_x] + [0] * (8 - self.parts))) for b in (0, 1)]
-        self._flag_ptrs = P(*([int(f.data_ptr()) for f in peer_flags] + [0] * (8 - self.parts)))
-        self._flags_local = peer_flags[self.rank]
-        self._peer_keep = (peer_x, peer_flags)
-        self.epoch = 0
+        ex = _Exchange()
+        ex.y_ptrs = [P(*([int(px[b].data_ptr()) for px in peer_x] + [0] * (8 - self.parts))) for b in (0, 1)]
+        ex.flag_ptrs = P(*([int(f.data_ptr()) for f in peer_flags] + [0] * (8 - self.parts)))
+        ex.flags_local = peer_flags[self.rank]
+        ex.keep = (peer_x, peer_flags)
+        ex.x = [peer_x[self.rank][0], peer_x[self.rank][1]]
+        self.p2p_attach(ex)
+
+    def p2p_attach(self, ex: "_Exchange") -> None:
+        """Use an existing exchange (buffers, peer mappings, flags and epoch counter),
+        e.g. the one of another PowerIteration over a matrix with the same row bounds:
+        the mappings do not depend on the matrix."""
+        self._ex = ex
+        self.x = ex.x
         self.p2p = True
 
     def p2p_connect(self, group=None) -> None:
@@ -223,7 +249,6 @@ class PowerIteration:
         fl = _device_view(self._owned[2], self.parts, torch.int64, self.device)
         xa.copy_(self.x[0])
         xb.copy_(self.x[1])
-        self.x = [xa, xb]
         allh = [None] * self.parts
         dist.all_gather_object(allh, mine, group=group)
         self._opened = []
@@ -242,44 +267,49 @@ class PowerIteration:
             peer_x.append((_PeerPtr(ptrs[0]), _PeerPtr(ptrs[1])))
             peer_flags.append(_PeerPtr(ptrs[2]))
         self.p2p_setup(peer_x, peer_flags)
-        self._group = group
+        self._ex.owned, self._ex.opened, self._ex.group = self._owned, self._opened, group
         dist.barrier(group=group)
 
     def close(self) -> None:
         """Unmap the peers' buffers, then (after every rank did) free this rank's."""
-        if not getattr(self, "_owned", None):
+        ex = getattr(self, "_ex", None)
+        if ex is None or not ex.owned:
             return
         import torch.distributed as dist
 
         self.torch.cuda.synchronize(self.device)
         L = self._lib.load()
-        for p in self._opened:
+        for p in ex.opened:
             L.tg_ipc_close(p)
-        self._opened = []
-        dist.barrier(group=self._group)
+        ex.opened = []
+        dist.barrier(group=ex.group)
         self.x = [self.x[0].clone(), self.x[1].clone()]
-        self._peer_keep = None
-        for p in self._owned:
+        ex.keep = None
+        for p in ex.owned:
             L.tg_peer_buffer_free(p)
-        self._owned = []
+        ex.owned = []
         self.p2p = False
 
     def p2p_step(self, src_index: int) -> None:
         """One fused step: read self.x[src_index], push into every rank's other buffer."""
         L = self._lib.load()
-        self.epoch += 1
+        ex = self._ex
+        ex.epoch += 1
         self._lib.check(L.tg_power_step_p2p_f64(ctypes.byref(self._desc), self.x[src_index].data_ptr(), self.parts,
-                                                self.rank, self.stride, self._y_ptrs[1 - src_index],
-                                                self._flag_ptrs, self.epoch, ctypes.byref(self._sched_c),
-                                                self.ws.data_ptr(), self.ws.numel(), self._stream()),
-                        "tg_power_step_p2p_f64")
+                                                self.rank, self.stride, ex.y_ptrs[1 - src_index], ex.flag_ptrs,
+                                                ex.epoch, ctypes.byref(self._sched_c), self.ws.data_ptr(),
+                                                self.ws.numel(), self._stream()), "tg_power_step_p2p_f64")
         self.kernel_launches += 1
 
     def p2p_wait(self) -> None:
         L = self._lib.load()
-        self._lib.check(L.tg_p2p_wait(self._flags_local.data_ptr(), self.parts, self.epoch, self.ws.data_ptr(),
-                                      self.ws.numel(), self._stream()), "tg_p2p_wait")
+        self._lib.check(L.tg_p2p_wait(self._ex.flags_local.data_ptr(), self.parts, self._ex.epoch,
+                                      self.ws.data_ptr(), self.ws.numel(), self._stream()), "tg_p2p_wait")
         self.kernel_launches += 1
+
+    @property
+    def exchange_state(self) -> "_Exchange":
+        return self._ex
 
     def error_word(self) -> int:
         L = self._lib.load()
