@@ -41,6 +41,17 @@ X0_SEED = 7
 ITERS = 20
 FALLBACK_HBM_GBS = 6650.0
 
+WORKLOADS = ("c4", "c1", "c2", "c3", "c5-spmm", "c5-sddmm")
+# Default schedule per workload: the fastest measured in the schedule sweeps on a B200.
+SCHEDULES = {
+    "c4": {"split": "rowwise", "tpr": 4, "unroll": 2, "vec": 2, "block": 256},
+    "c1": {"split": "rowwise", "tpr": 8, "unroll": 2, "vec": 2, "block": 256},
+    "c2": {"split": "rowwise", "tpr": 4, "unroll": 2, "vec": 2, "block": 128},
+    "c3": {"split": "merge", "tpr": 8, "unroll": 2, "vec": 2, "block": 128},
+    "c5-spmm": {"split": "merge", "tpr": 32, "unroll": 4, "vec": 4, "block": 128},
+    "c5-sddmm": {"split": "merge", "tpr": 8, "unroll": 1, "vec": 4, "block": 128},
+}
+
 
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -51,15 +62,24 @@ def parse():
     ap.add_argument("--rows", type=int, default=C4_N, help="matrix size (default: the C4 config)")
     ap.add_argument("--iters", type=int, default=ITERS)
     ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--split", choices=["stream", "rowwise"], default="rowwise")
+    ap.add_argument("--workload", choices=WORKLOADS, default="c4",
+                    help="c4: the power-iteration headline (default); c1/c2/c3: one SpMV per step; "
+                         "c5-spmm / c5-sddmm: one SpMM (K=128) / SDDMM (K=64) per step, fp32")
+    ap.add_argument("--split", choices=["stream", "rowwise", "merge"], default=None)
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: fused SpMV + peer-memory push (p2p) or NCCL all-gather")
-    ap.add_argument("--tpr", type=int, default=4)
-    ap.add_argument("--unroll", type=int, default=2)
-    ap.add_argument("--vec", type=int, default=2)
-    ap.add_argument("--block", type=int, default=256)
+    ap.add_argument("--tpr", type=int, default=None)
+    ap.add_argument("--unroll", type=int, default=None)
+    ap.add_argument("--vec", type=int, default=None)
+    ap.add_argument("--block", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--no-cusparse", action="store_true")
+    args = ap.parse_args()
+    d = SCHEDULES[args.workload]
+    for k in ("split", "tpr", "unroll", "vec", "block"):
+        if getattr(args, k) is None:
+            setattr(args, k, d[k])
+    return args
 
 
 def spmv_bytes(rows: int, cols: int, nnz: int) -> int:
@@ -243,6 +263,382 @@ def workload_config(n: int, world: int, exchange: str = "p2p"):
             "l2": "inputs (%.2f GB) larger than L2 (126 MB): no flush" % (spmv_bytes(n, n, n * C4_PER_ROW) / 1e9)}
 
 
+# ----------------------------------------------------------------------------- C1-C3, C5
+K_DENSE = {"c5-spmm": 128, "c5-sddmm": 64}
+INPUT_SEED = 11
+
+
+def matrix_kernel(workload: str) -> str:
+    return {"c5-spmm": "spmm", "c5-sddmm": "sddmm"}.get(workload, "spmv")
+
+
+def matrix_bytes(workload: str, A) -> int:
+    """Compulsory bytes of one call on the whole matrix: indptr + indices + values + dense
+    inputs + outputs, each once (8-byte indices; fp64 for SpMV, fp32 for C5)."""
+    M, N, nnz = A.rows, A.cols, A.nnz
+    if workload.startswith("c5"):
+        K = K_DENSE[workload]
+        base = 8 * (M + 1) + 12 * nnz
+        if workload == "c5-spmm":
+            return base + 4 * N * K + 4 * M * K
+        return base + 4 * M * K + 4 * N * K + 4 * nnz
+    return spmv_bytes(M, N, nnz)
+
+
+def matrix_flops(workload: str, A) -> float:
+    if workload.startswith("c5"):
+        return 2.0 * A.nnz * K_DENSE[workload] + (A.nnz if workload == "c5-sddmm" else 0)
+    return 2.0 * A.nnz
+
+
+def matrix_inputs(workload: str, A):
+    """Seeded U(-1,1) dense operands: x (fp64) for SpMV, B (N x 128) or U (M x 64),
+    V (N x 64) in fp32 for C5."""
+    rng = np.random.default_rng([INPUT_SEED, 0])
+    if workload == "c5-spmm":
+        return {"B": rng.uniform(-1.0, 1.0, size=(A.cols, 128)).astype(np.float32)}
+    if workload == "c5-sddmm":
+        U = rng.uniform(-1.0, 1.0, size=(A.rows, 64)).astype(np.float32)
+        V = rng.uniform(-1.0, 1.0, size=(A.cols, 64)).astype(np.float32)
+        return {"U": U, "V": V}
+    return {"x": rng.uniform(-1.0, 1.0, size=A.cols)}
+
+
+def row_shard(A, r0: int, r1: int):
+    from tilegen_b200.matrices import CSR
+
+    p0, p1 = int(A.indptr[r0]), int(A.indptr[r1])
+    return CSR(A.indptr[r0:r1 + 1] - p0, A.indices[p0:p1], A.data[p0:p1], (r1 - r0, A.cols),
+               "%s[%d:%d]" % (A.name, r0, r1))
+
+
+def matrix_config(workload: str, A, world: int, flush: bool):
+    desc = {"c1": "C1 uniform_random 100000^2, 16 distinct cols/row, fp64 SpMV",
+            "c2": "C2 banded 200000^2, offsets -3..3 clipped, fp64 SpMV",
+            "c3": "C3 power_law 100000^2, Zipf(2) rows scaled to mean 8, fp64 SpMV",
+            "c5-spmm": "C5 SpMM: power_law 1000000^2 (Zipf(2), mean 16) x dense 1000000x128, fp32",
+            "c5-sddmm": "C5 SDDMM: power_law 1000000^2 (Zipf(2), mean 16) pattern, U,V 1000000x64, fp32"}[workload]
+    return {"workload": desc, "rows": A.rows, "cols": A.cols, "nnz": A.nnz,
+            "max_row_nnz": int(np.diff(A.indptr).max()) if A.rows else 0,
+            "parallelism": "single GPU" if world == 1 else
+            "row-sharded x%d (nnz-balanced), dense operands replicated, no communication" % world,
+            "l2": ("host run" if flush is None else
+                   "L2 flushed (256 MB write) before every step, outside the step's events" if flush else
+                   "inputs larger than L2 (126 MB): no flush")}
+
+
+def cpu_reference_kernel(kernel: str, dtype: str):
+    """The reference's OpenMP launch_<kernel> (best of its three CPU configs on one call),
+    or None when the reference build is absent.  Returns (make_call, description)."""
+    from oracle import build as ob
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    if not os.path.exists(ob.GEN_DIR):
+        return None
+    libs = ob.rebuild_ref_native(os.path.join("/tmp", "tilegen_ref_native"))
+    march = "native"
+    if not libs:
+        libs, march = O.ref_omp_libs(), "x86-64-v3"
+    cands = [(cfg, libs["ref_omp_%s_%s_%s" % (kernel, dtype, cfg)]) for cfg in ("T32U1", "T64U2", "T128U4")
+             if "ref_omp_%s_%s_%s" % (kernel, dtype, cfg) in libs]
+    if not cands:
+        return None
+    return [(cfg, O.RefOmpKernel(path, kernel)) for cfg, path in cands], march, threads
+
+
+def cpu_matrix_caller(workload: str, A, inputs):
+    """A zero-argument call of the reference's OpenMP kernel on the whole matrix (its best
+    of three CPU configs, chosen once), else of the oracle's OpenMP SpMV port.  Returns
+    (call or None, kind, description, threads)."""
+    from oracle import oracle as O
+
+    kernel = matrix_kernel(workload)
+    dtype = "f32" if workload.startswith("c5") else "f64"
+    M, N, nnz = A.rows, A.cols, A.nnz
+    ip, ix = A.indptr, A.indices
+    d = A.data.astype(np.float32) if dtype == "f32" else A.data
+    if kernel == "spmv":
+        out = np.empty(M)
+        args = (ip, ix, d, inputs["x"], out, M, N, nnz)
+    elif kernel == "spmm":
+        out = np.zeros((M, 128), dtype=np.float32)
+        args = (ip, ix, d, inputs["B"], out, M, N, 128, nnz)
+    else:
+        out = np.zeros(nnz, dtype=np.float32)
+        args = (ip, ix, d, inputs["U"], inputs["V"], out, M, N, 64, nnz)
+    threads = os.cpu_count() or 1
+    ref = cpu_reference_kernel(kernel, dtype)
+    if ref is not None:
+        cands, march, threads = ref
+        best = None
+        for cfg, k in cands:
+            k(*args)
+            t0 = time.perf_counter()
+            k(*args)
+            dt = time.perf_counter() - t0
+            if best is None or dt < best[0]:
+                best = (dt, cfg, k)
+        _, cfg, k = best
+        return ((lambda: k(*args)), "reference",
+                "reference OpenMP launch_%s (tilegen codegen cpu backend, %s, %s, -O3 -march=%s -fopenmp)"
+                % (kernel, dtype, cfg, march), threads)
+    if kernel != "spmv":
+        return None, "port", "no reference OpenMP build of launch_%s on this host" % kernel, threads
+    x = inputs["x"]
+    return (lambda: O.spmv_omp(A, x, out=out)), "port", "oracle OpenMP port of cpp/src/ref.cpp:6-15", threads
+
+
+def cpu_matrix_sample(workload: str, A, inputs, reps: int):
+    """(seconds per whole-matrix call, kind, description, threads) over `reps` calls."""
+    call, kind, desc, threads = cpu_matrix_caller(workload, A, inputs)
+    if call is None:
+        return None, kind, desc, threads
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        call()
+    return (time.perf_counter() - t0) / reps, kind, desc, threads
+
+
+def run_matrix_reference(args, rank: int, world: int):
+    """--impl reference for C1-C3/C5: the reference's OpenMP kernel on the host cores, one
+    whole-matrix call per step, rank 0 only."""
+    if rank != 0:
+        return 0
+    from tilegen_b200 import matrices as Mx
+
+    A = Mx.baseline_matrix("c5" if args.workload.startswith("c5") else args.workload)
+    inputs = matrix_inputs(args.workload, A)
+    call, kind, desc, threads = cpu_matrix_caller(args.workload, A, inputs)
+    if call is None:
+        print(json.dumps({"impl": "reference", "unavailable": desc}), flush=True)
+        return 0
+    for _ in range(args.warmup):
+        call()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - t0)
+    sec = float(np.mean(times))
+    gbs = matrix_bytes(args.workload, A) / sec / 1e9
+    line = {"impl": "reference", "metric": "effective_hbm_gbs_" + matrix_kernel(args.workload), "value": round(gbs, 3),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(sec * 1e3, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32" if args.workload.startswith("c5") else "f64", "data": "synthetic (seeded generators)",
+            "config": matrix_config(args.workload, A, world, None),
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                             "sample": "one whole-matrix call per step", "impl": desc},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_matrix_workload(args, rank: int, world: int, local_rank: int):
+    """C1-C3 (one SpMV per step) and C5 (one SpMM or SDDMM per step), row-sharded over the
+    ranks with the dense operands replicated (strong scaling, no communication)."""
+    import torch
+    import torch.distributed as dist
+
+    from tilegen_b200 import device as D
+    from tilegen_b200 import lib, matrices as Mx
+    from tilegen_b200.power import nnz_balanced_bounds
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    L = lib.load()
+    wl = args.workload
+    kernel = matrix_kernel(wl)
+    c5 = wl.startswith("c5")
+    A = Mx.baseline_matrix("c5" if c5 else wl)
+    inputs = matrix_inputs(wl, A)
+    bounds = nnz_balanced_bounds(np.diff(A.indptr), world)
+    r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
+    S = row_shard(A, r0, r1)
+    dt = torch.float32 if c5 else torch.float64
+    Ad = D.DeviceCSR.from_host(S, dev, dt)
+
+    sch = lib.default_schedule()
+    sch.threads_per_row, sch.unroll, sch.vector_width, sch.block_size, sch.tile = (args.tpr, args.unroll, args.vec,
+                                                                                   args.block, 32)
+    sch.split = {"rowwise": lib.TG_SPLIT_ROWWISE, "merge": lib.TG_SPLIT_MERGE, "stream": lib.TG_SPLIT_STREAM}[args.split]
+    lib.validate_schedule(sch)
+
+    # pinned host inputs (e2e) and their device copies
+    h_in = {k: torch.from_numpy(np.ascontiguousarray(v[r0:r1] if k == "U" else v)).pin_memory()
+            for k, v in inputs.items()}
+    d_in = {k: v.to(dev, dtype=dt) for k, v in h_in.items()}
+    if kernel == "spmv":
+        out = torch.empty(S.rows, dtype=dt, device=dev)
+        step = lambda: D.spmv(Ad, d_in["x"], out, sched=sch)  # noqa: E731
+    elif kernel == "spmm":
+        out = torch.empty((S.rows, 128), dtype=dt, device=dev)
+        step = lambda: D.spmm(Ad, d_in["B"], out, sched=sch)  # noqa: E731
+    else:
+        out = torch.empty(S.nnz, dtype=dt, device=dev)
+        step = lambda: D.sddmm(Ad, d_in["U"], d_in["V"], out, sched=sch)  # noqa: E731
+    h_out = torch.empty(out.shape, dtype=dt).pin_memory()
+    flush_needed = matrix_bytes(wl, A) < (256 << 20)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if flush_needed else None
+    stream = torch.cuda.current_stream(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    barrier()
+    n0 = L.tg_launch_count()
+    evs = []
+    wall0 = time.perf_counter()
+    for _ in range(args.steps):
+        if flush is not None:
+            flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        evs.append((e0, e1))
+    barrier()
+    wall = time.perf_counter() - wall0
+    launches = L.tg_launch_count() - n0
+    clocks = sampler.stop() if sampler else None
+    ms_local = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+
+    # e2e through the public API: H2D of the step's dense inputs from pinned memory, the
+    # call, D2H of the output shard
+    e2e = []
+    for it in range(args.e2e_steps + 1 if args.e2e_steps > 0 else 0):
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in d_in:
+            d_in[k].copy_(h_in[k], non_blocking=True)
+        step()
+        h_out.copy_(out, non_blocking=True)
+        e1.record(stream)
+        barrier()
+        if it > 0:
+            e2e.append(e0.elapsed_time(e1))
+    e2e_local = float(np.mean(e2e)) if e2e else float("nan")
+
+    vals = torch.tensor([ms_local, e2e_local], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_step, e2e_ms = [float(v) for v in vals.cpu()]
+    total = matrix_bytes(wl, A)
+    gbs = total / (ms_step / 1e3) / 1e9
+
+    line = None
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        local_bytes = matrix_bytes(wl, S)  # this rank's rows, the whole replicated dense input
+        achieved = local_bytes / (ms_local / 1e3) / 1e9
+        kname = {"spmv": "spmv_rowwise_kernel" if args.split == "rowwise" else "spmv_merge_kernel",
+                 "spmm": "spmm kernel", "sddmm": "sddmm kernel"}[kernel]
+        tr = traffic_record("%s_%d" % (wl, world), kname)
+        h2d = int(sum(v.numel() * v.element_size() for v in h_in.values()))
+        line = {
+            "metric": "effective_hbm_gbs_" + kernel,
+            "value": round(gbs, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32" if c5 else "f64",
+            "data": "synthetic (seeded generators, values U(-1,1))",
+            "config": matrix_config(wl, A, world, flush is not None),
+            "gflops": round(matrix_flops(wl, A) / (ms_step / 1e3) / 1e9, 2),
+            "e2e": {"value": round(total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": int(h_out.numel() * h_out.element_size()), "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "peak_source": (peak_kind + " (MEASURED_PEAKS.json hbm_gbs)") if peak_kind == "measured"
+                         else "fallback 6.65 TB/s",
+                         "kernel": kname + " (whole call, every launch of the step)",
+                         "kernel_ms": round(ms_local, 5), "algorithmic_bytes_per_launch": int(local_bytes),
+                         "traffic": tr["dram_bytes_per_launch"] if tr else None},
+            "clocks": clocks,
+            "wall_s_timed": round(wall, 4),
+            "schedule": {"split": args.split, "tpr": args.tpr, "unroll": args.unroll, "vec": args.vec,
+                         "block": args.block},
+        }
+        if world == 1 and not args.no_cusparse:
+            line["cusparse"] = cusparse_compare(wl, Ad, d_in, flush, args.steps, total)
+    barrier()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            sec, kind, desc, threads = cpu_matrix_sample(wl, A, inputs, 3 if c5 else 20)
+            if sec is not None:
+                cg = matrix_bytes(wl, A) / sec / 1e9
+                line["cpu_baseline"] = {"value": round(cg, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                                        "sample": "%d whole-matrix calls on the host cores" % (3 if c5 else 20),
+                                        "impl": desc}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def cusparse_compare(workload: str, Ad, d_in, flush, steps: int, total_bytes: int):
+    """The same call through torch.sparse (cuSPARSE) on the same device arrays, timed the
+    same way; a comparison only, never part of the product path."""
+    import torch
+
+    try:
+        Sp = torch.sparse_csr_tensor(Ad.indptr, Ad.indices, Ad.data, size=(Ad.rows, Ad.cols))
+        if workload == "c5-spmm":
+            fn = lambda: torch.sparse.mm(Sp, d_in["B"])  # noqa: E731
+            op = "torch.sparse.mm (cusparseSpMM)"
+        elif workload == "c5-sddmm":
+            Vt = d_in["V"].t()
+            fn = lambda: torch.sparse.sampled_addmm(Sp, d_in["U"], Vt, beta=0.0, alpha=1.0)  # noqa: E731
+            op = "torch.sparse.sampled_addmm (cusparseSDDMM; without the A.val product)"
+        else:
+            xx = d_in["x"]
+            fn = lambda: torch.mv(Sp, xx)  # noqa: E731
+            op = "torch.mv on a CSR tensor (cusparseSpMV)"
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(steps):
+            if flush is not None:
+                flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            ts.append((a, b))
+        torch.cuda.synchronize()
+        ms = float(np.mean([a.elapsed_time(b) for a, b in ts]))
+        return {"op": op, "ms_per_step": round(ms, 5), "value": round(total_bytes / (ms / 1e3) / 1e9, 2),
+                "unit": "GB/s"}
+    except Exception as exc:  # noqa: BLE001 -- a comparison must not fail the bench
+        return {"error": str(exc)[:200]}
+
+
 # ----------------------------------------------------------------------------- b200 arm
 def main():
     args = parse()
@@ -250,7 +646,11 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if args.workload != "c4":
+            return run_matrix_reference(args, rank, world)
         return run_reference(args, rank, world)
+    if args.workload != "c4":
+        return run_matrix_workload(args, rank, world, local_rank)
 
     import torch
     import torch.distributed as dist

@@ -60,8 +60,8 @@ typedef void* tg_stream_t;
 /* Row-to-thread mapping of the kernels. */
 #define TG_SPLIT_ROWWISE 0 /* reference mapping: T rows per CTA tile, TPR lanes per row */
 #define TG_SPLIT_MERGE 1   /* nnz-balanced chunks, rows split across chunks + fix-up */
-#define TG_SPLIT_AUTO 2    /* library picks (stream when the operands allow it) */
-#define TG_SPLIT_STREAM 3  /* SpMV: persistent TMA-fed streaming kernel (nnz-balanced chunks) */
+#define TG_SPLIT_AUTO 2    /* library picks: the merge split (any row-length distribution) */
+#define TG_SPLIT_STREAM 3  /* SpMV: persistent TMA-fed row-block kernel; merge for SpMM/SDDMM */
 
 /* flags */
 #define TG_FLAG_BOUNDS_CHECK 1u /* validate indptr/indices on the device; TG_EBOUNDS on error */
@@ -80,7 +80,7 @@ typedef struct tg_sched {
     int32_t threads_per_row; /* TPR: lanes cooperating on one row (ThreadsPerRow)        */
     int32_t unroll;          /* U: independent loads in flight per lane (Unroll)          */
     int32_t vector_width;    /* V: elements per vector load (Vectorize)                   */
-    int32_t block_size;      /* B: threads per CTA (Parallelize block_size)               */
+    int32_t block_size;      /* B: threads per CTA (Parallelize block_size), 32..512      */
     int32_t split;           /* TG_SPLIT_*                                                */
     int32_t chunk_nnz;       /* merge split: nonzeros per chunk (0 = library default)     */
     uint32_t flags;          /* TG_FLAG_*                                                 */
@@ -102,6 +102,10 @@ TG_API const char* tg_version(void);
 TG_API const char* tg_last_error_string(void);
 /* Status of the last reference-compatible launch_* call on this host thread. */
 TG_API int tg_last_status(void);
+/* Number of kernels this library has launched in the process so far (all threads and
+ * devices; memsets and copies are not kernels).  Benchmarks difference it around a
+ * timed region. */
+TG_API uint64_t tg_launch_count(void);
 /* Fills *s with the library defaults (reference BASELINE T32/TPR1/U1/V1/B128,
  * tilegen/autotune.py:55-56, with split = TG_SPLIT_ROWWISE). */
 TG_API void tg_default_schedule(tg_sched* s);

@@ -17,7 +17,7 @@ def test_library_loads_and_reports_version():
 
 def test_every_header_symbol_is_exported_and_typed():
     declared = set(lib.header_symbols())
-    assert len(declared) == 36
+    assert len(declared) == 37
     assert declared == set(lib.SIGNATURES)
     out = subprocess.run(["nm", "-D", "--defined-only", lib.lib_path()], capture_output=True, text=True).stdout
     exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
@@ -49,6 +49,7 @@ def test_default_schedule_is_reference_baseline():
     ("unroll", 3, "unroll"),
     ("vector_width", 8, "vector_width"),
     ("block_size", 100, "block_size"),
+    ("block_size", 1024, "block_size"),
     ("split", 7, "split"),
 ])
 def test_invalid_schedules_are_rejected(field, value, msg):

@@ -21,7 +21,9 @@ def test_config_hash_matches_reference_formula_for_shared_knobs():
 def test_lowering_rules_for_standard_kernels():
     cfg = cg.Config(tile_size=128, threads_per_row=8, unroll=4, vector_width=2, block_size=512)
     spmv = cg.lower("spmv", cfg)
-    assert (spmv.tile, spmv.threads_per_row, spmv.unroll, spmv.vector_width, spmv.block_size) == (128, 8, 4, 1, 512)
+    # V is kept for SpMV too: the b200 template loads the CSR stream V-wide (the
+    # reference drops it there because its SpMV template has nothing to vectorise)
+    assert (spmv.tile, spmv.threads_per_row, spmv.unroll, spmv.vector_width, spmv.block_size) == (128, 8, 4, 2, 512)
     spmm = cg.lower("spmm", cfg)
     assert spmm.vector_width == 2  # rank-2 dense access keeps Vectorize
     t1 = cg.lower("spmv", cg.Config(tile_size=1, threads_per_row=1))
@@ -67,8 +69,12 @@ def test_lowering_from_reference_schedule_objects():
     k = Kernel("spmv", [Tile(64), Parallelize(256), ThreadsPerRow(4), Unroll(2), Vectorize(2)], [{"pass": "x"}])
     g = cg.generate_from_lowered(k, cg.Config())
     assert (g.lowering.tile, g.lowering.threads_per_row, g.lowering.unroll, g.lowering.block_size) == (64, 4, 2, 256)
-    assert g.lowering.vector_width == 1  # SpMV gather: not vectorised, as in the reference
+    assert g.lowering.vector_width == 2
     assert g.pass_log == [{"pass": "x"}]
+    # the reference pipeline drops Vectorize for SpMV: V then comes from the config
+    k2 = Kernel("spmv", [Tile(64), Parallelize(256), ThreadsPerRow(4), Unroll(2)], [])
+    assert cg.generate_from_lowered(k2, cg.Config(vector_width=4)).lowering.vector_width == 4
+    assert cg.generate_from_lowered(k2, cg.Config()).lowering.vector_width == 1
     with pytest.raises(NotImplementedError):
         cg.generate_from_lowered(Kernel("mystery", [], []), cg.Config())
 

@@ -72,7 +72,7 @@ class Config:
 
     ``split`` chooses the row mapping of the b200 kernels ("rowwise": the reference's
     T/TPR mapping; "merge": nnz-balanced chunks; "stream": the persistent TMA-fed SpMV,
-    merge for SpMM/SDDMM; "auto": stream), ``chunk_nnz`` the merge chunk size for
+    merge for SpMM/SDDMM; "auto": merge), ``chunk_nnz`` the merge chunk size for
     SpMM/SDDMM, ``bounds_check`` a device-side CSR validation before the call."""
 
     tile_size: int = 32
@@ -144,8 +144,10 @@ def lower(kernel_name: str, config: Config, skip_passes: Sequence[str] = ()) -> 
     tiling (tilegen/passes.py:243-270): Tile(T) when T > 1;
     thread_mapping (:276-316): Parallelize(block=B), ThreadsPerRow(TPR) when TPR > 1;
     unroll (:322-342): Unroll(U) when U > 1;
-    vectorize (:348-396): Vectorize(V) when V > 1 and the kernel has a rank-2 dense
-    access (SpMM, SDDMM); the dense extent K is symbolic, so no divisibility pruning.
+    vectorize (:348-396): Vectorize(V) when V > 1.  The reference keeps Vectorize only
+    for kernels with a rank-2 dense access (SpMM, SDDMM), because its emitted SpMV
+    template has nothing to vectorise; the b200 SpMV template reads the CSR stream
+    (indices, values) with V-wide vector loads, so V is kept for every kernel.
     A skipped pass leaves its knob at the Lowering default, as in the reference.
     """
     if kernel_name not in STANDARD_KERNELS:
@@ -161,7 +163,7 @@ def lower(kernel_name: str, config: Config, skip_passes: Sequence[str] = ()) -> 
             low.threads_per_row = config.threads_per_row
     if "unroll" not in skip and config.unroll > 1:
         low.unroll = config.unroll
-    if "vectorize" not in skip and config.vector_width > 1 and kernel_name in _HAS_2D_DENSE:
+    if "vectorize" not in skip and config.vector_width > 1:
         low.vector_width = config.vector_width
     return low
 
@@ -268,8 +270,10 @@ def generate_from_lowered(optimized_kernel, config: Config) -> B200Kernel:
     if name not in STANDARD_KERNELS:
         raise NotImplementedError("the b200 backend has kernels for %s (got %r)" % (sorted(STANDARD_KERNELS), name))
     low = lowering_from_schedule(optimized_kernel.schedule, config.split, config.chunk_nnz)
-    if name not in _HAS_2D_DENSE:
-        low.vector_width = 1
+    if name not in _HAS_2D_DENSE and low.vector_width == 1:
+        # the reference's vectorize pass dropped V for a kernel without a rank-2 dense
+        # access; the b200 template vectorises the CSR stream, so take V from the config
+        low.vector_width = max(1, int(config.vector_width))
     return B200Kernel(name, config, low, STANDARD_KERNELS[name],
                       pass_log=list(getattr(optimized_kernel, "pass_log", []) or []))
 

@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -34,7 +35,14 @@ int check_cuda(cudaError_t e, const char* what) {
     return set_error(TG_ECUDA, "%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
 }
 
-int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+// Every kernel launch site calls check_launch right after its <<<...>>>, so this is
+// also where launches are counted (tg_launch_count).
+std::atomic<uint64_t> g_launches{0};
+
+int check_launch(const char* what) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_cuda(cudaGetLastError(), what);
+}
 
 // kernels defined in tg_spmv.cu
 template <typename T, bool AXPY>
@@ -111,7 +119,9 @@ int resolve(const tg_sched* in, tg_sched* out) {
     if (s.unroll <= 0) s.unroll = 1;
     if (s.vector_width <= 0) s.vector_width = 1;
     if (s.block_size <= 0) s.block_size = 128;
-    if (s.split == TG_SPLIT_AUTO) s.split = TG_SPLIT_STREAM;
+    // AUTO: the host does not see the row lengths, so take the mapping that is
+    // load-balanced for every distribution (rowwise is the tuned choice for regular rows)
+    if (s.split == TG_SPLIT_AUTO) s.split = TG_SPLIT_MERGE;
     const int tpr = s.threads_per_row;
     if (tpr != 1 && tpr != 2 && tpr != 4 && tpr != 8 && tpr != 16 && tpr != 32)
         return set_error(TG_EINVAL, "threads_per_row must be 1, 2, 4, 8, 16 or 32 (got %d)", tpr);
@@ -119,8 +129,10 @@ int resolve(const tg_sched* in, tg_sched* out) {
         return set_error(TG_EINVAL, "unroll must be 1, 2, 4 or 8 (got %d)", s.unroll);
     if (s.vector_width != 1 && s.vector_width != 2 && s.vector_width != 4)
         return set_error(TG_EINVAL, "vector_width must be 1, 2 or 4 (got %d)", s.vector_width);
-    if (s.block_size < 32 || s.block_size > 1024 || s.block_size % 32 != 0)
-        return set_error(TG_EINVAL, "block_size must be a multiple of 32 in [32, 1024] (got %d)", s.block_size);
+    // the row kernels are compiled for at most 512 threads per CTA (up to 128 registers a
+    // thread, so no instance spills); the reference's space tops out at 512 too
+    if (s.block_size < 32 || s.block_size > 512 || s.block_size % 32 != 0)
+        return set_error(TG_EINVAL, "block_size must be a multiple of 32 in [32, 512] (got %d)", s.block_size);
     if (s.block_size % tpr != 0)
         return set_error(TG_EINVAL, "block_size (%d) not divisible by threads_per_row (%d)", s.block_size, tpr);
     if (s.split != TG_SPLIT_ROWWISE && s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_STREAM)
@@ -203,6 +215,8 @@ const char* tg_version(void) { return "tilegen_b200 0.1.0 (sm_100a)"; }
 const char* tg_last_error_string(void) { return t_msg; }
 
 int tg_last_status(void) { return t_last_status; }
+
+uint64_t tg_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 void tg_default_schedule(tg_sched* s) {
     if (s) *s = tg_sched{32, 1, 1, 1, 128, TG_SPLIT_ROWWISE, 0, 0u};

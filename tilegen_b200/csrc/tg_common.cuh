@@ -128,6 +128,32 @@ __device__ __forceinline__ T ld_cg(const T* p) {
     return __ldcg(p);
 }
 
+// Sum of the partials p[0], p[stride], ..., p[(n-1)*stride] added in index order into s.
+// The loads are issued eight at a time (independent, all in flight together) and the
+// adds stay in order, so the result is the same as the one-at-a-time loop but the
+// latency is paid once per eight partials instead of once per partial.
+template <typename T, class SUM>
+__device__ __forceinline__ void add_partials(SUM& s, const T* p, int64_t n, int64_t stride) {
+    int64_t c = 0;
+    for (; c + 8 <= n; c += 8) {
+        T v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = ld_cg(p + (c + k) * stride);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s.add(v[k]);
+    }
+    for (; c < n; ++c) s.add(ld_cg(p + c * stride));
+}
+
+// ------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialisation may start while the kernel
+// before it on the stream is still running.  The earlier kernel calls pdl_trigger() to
+// let it start; the later one calls pdl_wait() before it reads anything the earlier
+// kernel writes (pdl_wait returns once that kernel has completed and its writes are
+// visible, and at once when there is no such dependency).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------ TMA bulk copies
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -108,7 +108,7 @@ __device__ __forceinline__ void split_arrive_rows(const DenseArgs<T>& a, int64_t
                     const int64_t col = col0 + e;
                     Sum<T> s;
                     s.add(ld_cg(&a.tail[ca * a.kpart + col]));
-                    for (int64_t c = ca + 1; c <= cb; ++c) s.add(ld_cg(&a.head[c * a.kpart + col]));
+                    add_partials(s, a.head + (ca + 1) * a.kpart + col, cb - ca, a.kpart);
                     if (row < a.row_limit) a.C[row * a.ld + col] = s.get();
                 }
             }

@@ -74,7 +74,7 @@ __device__ __forceinline__ void grid_sum_last(double part, double* partials, uns
 }
 
 template <int TPR, int U, int V>
-__global__ void __launch_bounds__(1024) power_step_kernel(PowerArgs a) {
+__global__ void __launch_bounds__(512) power_step_kernel(PowerArgs a) {
     __shared__ double s_warp[32];
     __shared__ double s_scale;
     const uint64_t ps = policy_evict_first();

@@ -5,6 +5,7 @@ namespace tg {
 
 __global__ void partition_kernel(const int64_t* __restrict__ indptr, int64_t rows, int64_t S, int64_t nchunks,
                                  int64_t* __restrict__ own_first, int* __restrict__ cnt, uint32_t* err) {
+    pdl_trigger();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     for (int64_t r = tid; r <= rows; r += stride) {

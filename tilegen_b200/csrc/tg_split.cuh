@@ -10,12 +10,13 @@
 // over indptr (partition_kernel), which is the only "analysis" the merge path needs.
 //
 // A row whose nonzeros cross chunk boundaries (a SPLIT row spanning chunks ca..cb) gets
-// one partial sum per chunk: tail[ca] from its owner, head[c] from each later chunk.
-// Every contributor publishes its partial, fences, and arrives on cnt[ca]; the last of
-// the (cb - ca + 1) arrivals sums tail[ca] + head[ca+1] + ... + head[cb] in that fixed
-// order and writes the row.  The result is deterministic and needs no second launch.
-// The last arrival also resets cnt[ca] to zero, so the counters are left clean for the
-// next call on the same workspace.
+// one partial sum per chunk: tail[ca] from its owner, head[c] from each later chunk, and
+// the row is tail[ca] + head[ca+1] + ... + head[cb] in that fixed order (deterministic).
+// SpMV publishes the partials and sums them in a fix-up kernel launched right behind the
+// merge kernel (cnt[c] then holds the index of chunk c's split row).  SpMM/SDDMM, whose
+// CTAs are long-lived, sum them in place: every contributor publishes its partial,
+// fences and arrives on cnt[ca], and the last of the (cb - ca + 1) arrivals adds them
+// and writes the row; it also resets cnt[ca] to zero.
 #pragma once
 
 #include "tg_common.cuh"
@@ -55,29 +56,13 @@ inline SplitWs split_ws_carve(void* base, int64_t nchunks, int64_t width, size_t
 
 // One thread per row boundary r in [0, rows]: sets own_first[c] for every chunk c
 // whose first position c*S lies in (indptr[r-1], indptr[r]]; zeroes the arrival
-// counters and the error word.
+// counters and the error word.  It lets a kernel launched after it with programmatic
+// serialisation start at once (that kernel waits with pdl_wait before reading the table).
 __global__ void partition_kernel(const int64_t* __restrict__ indptr, int64_t rows, int64_t S, int64_t nchunks,
                                  int64_t* __restrict__ own_first, int* __restrict__ cnt, uint32_t* err);
 
 // Host launcher (defined in tg_split.cu).
 int launch_partition(const int64_t* indptr, int64_t rows, int64_t nnz, int64_t S, const SplitWs& ws,
                      cudaStream_t stream);
-
-// Arrival of one contributor of split row `row` (spanning chunks ca..cb) whose partial
-// has already been stored.  Scalar partials (SpMV).
-template <typename T, class EPI>
-__device__ __forceinline__ void split_arrive_scalar(int64_t row, int64_t ca, int64_t cb, int* cnt, const T* head,
-                                                    const T* tail, T* y, const EPI& epi, int64_t row_limit) {
-    __threadfence();
-    const int old = atomicAdd(&cnt[ca], 1);
-    if (old == (int)(cb - ca)) {
-        __threadfence();
-        Sum<T> s;
-        s.add(ld_cg(&tail[ca]));
-        for (int64_t c = ca + 1; c <= cb; ++c) s.add(ld_cg(&head[c]));
-        if (row < row_limit) y[row] = epi(s.get(), row);
-        cnt[ca] = 0;
-    }
-}
 
 }  // namespace tg

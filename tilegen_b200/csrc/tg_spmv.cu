@@ -10,14 +10,14 @@
 //    mask, so tails are well defined), each lane keeps U vector loads of V nonzeros in
 //    flight, indices/values stream with an L2 evict_first policy and x is gathered with
 //    evict_last.  Template parameters: TPR, U, V; runtime: T, B.
-//  * merge    -- nnz-balanced chunks of S = B*I nonzeros per CTA.  The chunk's indices
-//    and values are staged into shared memory by one TMA bulk copy (cp.async.bulk +
-//    mbarrier), row offsets by coalesced loads; each thread multiplies I consecutive
-//    nonzeros (all gathers in flight at once) and then walks them against the row
-//    offsets (merge of row ends and nonzero positions).  Rows crossing thread
-//    boundaries are summed by their owner thread; rows crossing chunk boundaries use
-//    the deterministic last-arriver protocol of tg_split.cuh.  Power-law rows of any
-//    length cost the same per nonzero as short rows.
+//  * merge    -- nnz-balanced chunks of S = B*I nonzeros per CTA.  The CTA computes
+//    the chunk's products into shared memory (I coalesced loads and I gathers in flight
+//    per thread), then sums each row's piece from shared memory: short pieces by one
+//    thread, long ones by a warp.  A row crossing chunk boundaries gets
+//    one partial per chunk, which a small fix-up kernel launched right behind (with
+//    programmatic serialisation, so its launch overlaps the merge kernel) adds in chunk
+//    order.  Power-law rows of any length cost the same per nonzero as short rows, and
+//    no CTA waits on a fence or an atomic.
 #include <algorithm>
 
 #include "tg_rowdot.cuh"
@@ -47,7 +47,7 @@ struct SpmvArgs {
 };
 
 template <typename T, int TPR, int U, int V, bool AXPY>
-__global__ void __launch_bounds__(1024) spmv_rowwise_kernel(SpmvArgs<T> a, Epi<T, AXPY> epi) {
+__global__ void __launch_bounds__(512) spmv_rowwise_kernel(SpmvArgs<T> a, Epi<T, AXPY> epi) {
     const uint64_t ps = policy_evict_first();
     const uint64_t pg = policy_evict_last();
     const int lane = threadIdx.x % TPR;
@@ -69,173 +69,146 @@ __global__ void __launch_bounds__(1024) spmv_rowwise_kernel(SpmvArgs<T> a, Epi<T
 }
 
 // ------------------------------------------------------------------ merge
-constexpr int kMergeI = 7;  // nonzeros per thread; odd => conflict-free 8-byte smem reads
+constexpr int kMergeI = 7;  // nonzeros per thread
 
+// Rows whose piece of a chunk is at most this long are summed by one thread; longer
+// pieces by a whole warp.
+constexpr int kShortPiece = 16;
+
+// Chunk c holds nonzeros [c*S, c*S + S) with S = B*I.  Its CTA
+//  1. computes the S products data[q] * x[indices[q]] into shared memory (each thread
+//     keeps I coalesced loads and then I gathers in flight);
+//  2. reads the offsets of the rows that start in the chunk (partition table);
+//  3. sums every row piece from shared memory in index order: short pieces by one
+//     thread, long pieces by a warp (strided partial sums, then a fixed shuffle tree).
+// A row that lies inside the chunk is written to y.  The piece of a row that started
+// in an earlier chunk (the chunk's head) and the piece of the chunk's last row when it
+// continues into later chunks (its tail) are published as partials for the fix-up
+// kernel.  Step 1 does not need the partition table, so it overlaps the partition
+// kernel (programmatic launch); the CTA never waits on another CTA.
 template <typename T, bool AXPY, int B>
 __global__ void __launch_bounds__(B) spmv_merge_kernel(SpmvArgs<T> a, Epi<T, AXPY> epi) {
     constexpr int I = kMergeI;
     constexpr int S = B * I;
     constexpr int RCAP = S + 32;
-    __shared__ alignas(128) unsigned char s_raw[S * 8 + S * sizeof(T)];
-    __shared__ alignas(16) int64_t s_off[RCAP];
-    __shared__ alignas(8) uint64_t s_bar;
-    int64_t* s_idx = reinterpret_cast<int64_t*>(s_raw);
-    T* s_val = reinterpret_cast<T*>(s_raw + S * 8);
+    constexpr int NW = B / kWarp;
+    __shared__ T s_prod[S];
+    __shared__ int64_t s_off[RCAP];
+    __shared__ int s_long[S / kShortPiece + 2];
+    __shared__ int s_nlong;
 
     const int tid = threadIdx.x;
     const int64_t c = blockIdx.x;
     const int64_t cs = c * S;
     const int64_t ce = min(cs + (int64_t)S, a.nnz);
-    const int64_t n_items = ce - cs;
+    const int n_items = (int)(ce - cs);
     const uint64_t ps = policy_evict_first();
     const uint64_t pg = policy_evict_last();
+    pdl_trigger();  // the fix-up kernel behind this one may be scheduled now
 
-    // 1. stage this chunk's indices and values: one TMA bulk copy each (16-byte granules),
-    //    the few trailing elements with plain loads.
-    constexpr int64_t kGran = (sizeof(T) == 4) ? 4 : 2;
-    const int64_t n_bulk = a.use_bulk ? (n_items / kGran) * kGran : 0;
-    if (tid == 0) {
-        mbar_init(&s_bar, 1);
-        fence_mbar_init();
-        if (n_bulk > 0) {
-            const uint32_t bi = (uint32_t)(n_bulk * 8);
-            const uint32_t bv = (uint32_t)(n_bulk * sizeof(T));
-            mbar_arrive_expect_tx(&s_bar, bi + bv);
-            bulk_g2s(s_idx, a.indices + cs, bi, &s_bar, ps);
-            bulk_g2s(s_val, a.data + cs, bv, &s_bar, ps);
-        } else {
-            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&s_bar)) : "memory");
+    // 1. products
+    {
+        int64_t col[I];
+        T val[I];
+#pragma unroll
+        for (int k = 0; k < I; ++k) {
+            const int q = tid + k * B;
+            col[k] = 0;
+            val[k] = T(0);
+            if (q < n_items) {
+                col[k] = ld_stream(a.indices + cs + q, ps);
+                val[k] = ld_stream(a.data + cs + q, ps);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < I; ++k) {
+            const int q = tid + k * B;
+            if (q < n_items) s_prod[q] = val[k] * ld_gather(a.x + col[k], pg);
         }
     }
-    for (int64_t k = n_bulk + tid; k < n_items; k += B) {
-        s_idx[k] = ld_stream(a.indices + cs + k, ps);
-        s_val[k] = ld_stream(a.data + cs + k, ps);
-    }
+    if (tid == 0) s_nlong = 0;
 
-    // 2. row offsets touching the chunk: indptr[r_lo .. r_hi+1]
+    // 2. offsets of the rows starting in the chunk: indptr[of0 .. of1].  The partition
+    //    table is written by the kernel launched just before this one, so wait for it.
+    pdl_wait();
     const int64_t of0 = a.own_first[c];
     const int64_t of1 = a.own_first[c + 1];
-    const int64_t r_lo = of0 > 0 ? of0 - 1 : 0;
-    const int64_t r_hi = of1 - 1;
-    const int64_t n_off = r_hi + 2 - r_lo;
+    const int64_t n_off = of1 - of0 + 1;
     const bool off_smem = n_off <= RCAP;
     if (off_smem)
-        for (int64_t j = tid; j < n_off; j += B) s_off[j] = a.indptr[r_lo + j];
+        for (int64_t j = tid; j < n_off; j += B) s_off[j] = a.indptr[of0 + j];
     __syncthreads();
-    if (!mbar_wait(&s_bar, 0)) {
-        if (tid == 0) atomicOr(a.err, 1u);
-        return;
-    }
-    const int64_t* off = off_smem ? s_off : (a.indptr + r_lo);
+    const int64_t* off = off_smem ? s_off : (a.indptr + of0);
 
-    // 3. products of this thread's I nonzeros, then the merge walk
-    const int64_t qa = cs + (int64_t)tid * I;
-    const int64_t qb = min(qa + (int64_t)I, ce);
-    int64_t h_row = -1, t_row = -1;
-    T h_val = T(0), t_val = T(0);
-    if (qa < qb) {
-        T prod[I];
-#pragma unroll
-        for (int k = 0; k < I; ++k) {
-            const int64_t q = qa + k;
-            prod[k] = T(0);
-            if (q < qb) {
-                const int64_t li = q - cs;
-                prod[k] = s_val[li] * ld_gather(a.x + s_idx[li], pg);
-            }
-        }
-        // first row of the walk: empty rows starting exactly at qa, else the row containing qa
-        int64_t lo = 0, hi = n_off;
-        while (lo < hi) {
-            const int64_t mid = (lo + hi) >> 1;
-            if (off[mid] < qa)
-                lo = mid + 1;
-            else
-                hi = mid;
-        }
-        int64_t j = (lo < n_off && off[lo] == qa) ? lo : lo - 1;
-        const bool head = off[j] < qa;
-        bool first = true;
-        Sum<T> acc;
-        int64_t nxt = off[j + 1];
-#pragma unroll
-        for (int k = 0; k < I; ++k) {
-            const int64_t q = qa + k;
-            if (q < qb) {
-                while (nxt <= q) {
-                    const int64_t r = r_lo + j;
-                    if (first && head) {
-                        h_row = r;
-                        h_val = acc.get();
-                    } else if (r < a.row_limit) {
-                        a.y[r] = epi(acc.get(), r);
-                    }
-                    first = false;
-                    acc = Sum<T>();
-                    ++j;
-                    nxt = off[j + 1];
-                }
-                acc.add(prod[k]);
-            }
-        }
-        const int64_t r = r_lo + j;
-        if (nxt == qb) {
-            if (first && head) {
-                h_row = r;
-                h_val = acc.get();
-            } else if (r < a.row_limit) {
-                a.y[r] = epi(acc.get(), r);
-            }
-            if (qb == a.nnz)  // trailing empty rows (start == end == nnz)
-                for (int64_t rr = r + 1; rr < a.rows && rr < a.row_limit; ++rr) a.y[rr] = epi(T(0), rr);
-        } else if (first && head) {
-            h_row = r;  // the whole range lies inside one row that started earlier
-            h_val = acc.get();
+    // 3. pieces: task 0 is the head (rows before of0 continuing into the chunk), task
+    //    1 + j is row of0 + j.  Piece [lo, hi) in chunk coordinates.
+    const int64_t ntask = n_off;  // head + (of1 - of0) rows
+    auto piece = [&](int64_t t, int& lo, int& hi) {
+        if (t == 0) {
+            lo = 0;
+            hi = (int)(min(off[0], ce) - cs);
         } else {
-            t_row = r;
-            t_val = acc.get();
+            lo = (int)(off[t - 1] - cs);
+            hi = (int)(min(off[t], ce) - cs);
         }
+    };
+    auto finish = [&](int64_t t, T v) {
+        if (t == 0) {
+            a.head[c] = v;
+        } else {
+            const int64_t r = of0 + t - 1;
+            if (off[t] <= ce) {
+                if (r < a.row_limit) a.y[r] = epi(v, r);
+            } else {
+                a.tail[c] = v;  // the chunk's last row continues past the chunk
+                a.cnt[c] = (int)t;
+            }
+        }
+    };
+    for (int64_t t = tid; t < ntask; t += B) {
+        int lo, hi;
+        piece(t, lo, hi);
+        if (t == 0 && hi <= 0) continue;  // no head
+        if (hi - lo > kShortPiece) {
+            s_long[atomicAdd(&s_nlong, 1)] = (int)t;
+            continue;
+        }
+        Sum<T> sum;
+        for (int q = lo; q < hi; ++q) sum.add(s_prod[q]);
+        finish(t, sum.get());
     }
+    __syncthreads();
+    const int nlong = s_nlong;
+    const int warp = tid / kWarp, lane = tid % kWarp;
+    for (int i = warp; i < nlong; i += NW) {
+        const int64_t t = s_long[i];
+        int lo, hi;
+        piece(t, lo, hi);
+        Sum<T> sum;
+        for (int q = lo + lane; q < hi; q += kWarp) sum.add(s_prod[q]);
+        const T v = group_sum<kWarp>(sum.get(), kFull);
+        if (lane == 0) finish(t, v);
+    }
+}
 
-    // 4. combine rows crossing thread boundaries (owner thread sums in thread order)
-    __syncthreads();
-    int64_t* s_hrow = reinterpret_cast<int64_t*>(s_raw);
-    int64_t* s_trow = s_hrow + B;
-    T* s_hval = reinterpret_cast<T*>(s_trow + B);
-    T* s_tval = s_hval + B;
-    s_hrow[tid] = h_row;
-    s_trow[tid] = t_row;
-    s_hval[tid] = h_val;
-    s_tval[tid] = t_val;
-    __syncthreads();
-    if (t_row >= 0) {
+// Rows split across chunks: chunk c's tail partial plus the head partials of the chunks
+// c+1..cb that the row covers, added in that order (the sums the merge kernel published),
+// one thread per chunk.  Launched right behind the merge kernel with programmatic
+// serialisation; everything before pdl_wait overlaps the merge kernel.
+template <typename T, bool AXPY>
+__global__ void __launch_bounds__(256) spmv_fixup_kernel(SpmvArgs<T> a, Epi<T, AXPY> epi, int64_t nchunks,
+                                                          int64_t S) {
+    pdl_wait();
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks;
+         c += (int64_t)gridDim.x * blockDim.x) {
+        const int code = a.cnt[c];  // 1 + the split row's index among the chunk's own rows
+        if (code == 0) continue;
+        const int64_t r = a.own_first[c] + code - 1;
+        const int64_t cb = (a.indptr[r + 1] - 1) / S;
         Sum<T> sum;
-        sum.add(t_val);
-        int u = tid + 1;
-        while (u < B && s_hrow[u] == t_row) {
-            sum.add(s_hval[u]);
-            ++u;
-        }
-        const int64_t row_end = off[t_row - r_lo + 1];
-        if (row_end <= ce) {
-            if (t_row < a.row_limit) a.y[t_row] = epi(sum.get(), t_row);
-        } else {
-            a.tail[c] = sum.get();
-            split_arrive_scalar(t_row, c, (row_end - 1) / S, a.cnt, a.head, a.tail, a.y, epi, a.row_limit);
-        }
-    }
-    if (tid == 0 && s_hrow[0] >= 0) {
-        const int64_t H = s_hrow[0];
-        Sum<T> sum;
-        sum.add(s_hval[0]);
-        int u = 1;
-        while (u < B && s_hrow[u] == H) {
-            sum.add(s_hval[u]);
-            ++u;
-        }
-        a.head[c] = sum.get();
-        const int64_t jh = H - r_lo;
-        split_arrive_scalar(H, off[jh] / S, (off[jh + 1] - 1) / S, a.cnt, a.head, a.tail, a.y, epi, a.row_limit);
+        sum.add(a.tail[c]);
+        add_partials(sum, a.head + c + 1, cb - c, 1);
+        if (r < a.row_limit) a.y[r] = epi(sum.get(), r);
     }
 }
 
@@ -370,11 +343,27 @@ int spmv_run(const tg_csr& A, const T* x, T* y, const Epi<T, AXPY>& epi, const t
         a.err = w.err;
         a.use_bulk = aligned16(A.indices) && aligned16(A.data);
         if (nchunks > 0x7fffffff) return set_error(TG_EINVAL, "too many chunks (%lld)", (long long)nchunks);
-        if (B == 128)
-            spmv_merge_kernel<T, AXPY, 128><<<(unsigned)nchunks, 128, 0, st>>>(a, epi);
-        else
-            spmv_merge_kernel<T, AXPY, 256><<<(unsigned)nchunks, 256, 0, st>>>(a, epi);
-        return check_launch("spmv_merge_kernel");
+        // programmatic launch: the chunk staging of the merge kernel overlaps the partition
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.gridDim = dim3((unsigned)nchunks);
+        cfg.blockDim = dim3((unsigned)B);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = B == 128 ? cudaLaunchKernelEx(&cfg, spmv_merge_kernel<T, AXPY, 128>, a, epi)
+                                 : cudaLaunchKernelEx(&cfg, spmv_merge_kernel<T, AXPY, 256>, a, epi);
+        if (e != cudaSuccess) return check_cuda(e, "spmv_merge_kernel launch");
+        rc = check_launch("spmv_merge_kernel");
+        if (rc != TG_OK) return rc;
+        cfg.gridDim = dim3((unsigned)std::min<int64_t>(ceil_div(nchunks, 256), 148 * 8));
+        cfg.blockDim = dim3(256);
+        e = cudaLaunchKernelEx(&cfg, spmv_fixup_kernel<T, AXPY>, a, epi, nchunks, S);
+        if (e != cudaSuccess) return check_cuda(e, "spmv_fixup_kernel launch");
+        return check_launch("spmv_fixup_kernel");
     }
     // rowwise
     const int tpr = s.threads_per_row;

@@ -95,6 +95,7 @@ SIGNATURES = {
     "tg_version": (ctypes.c_char_p, []),
     "tg_last_error_string": (ctypes.c_char_p, []),
     "tg_last_status": (ctypes.c_int, []),
+    "tg_launch_count": (ctypes.c_uint64, []),
     "tg_default_schedule": (None, [_SP]),
     "tg_validate_schedule": (ctypes.c_int, [_SP]),
     "tg_set_schedule": (ctypes.c_int, [_SP]),
