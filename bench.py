@@ -744,6 +744,37 @@ def main():
     kdur = [evs[2 * k].elapsed_time(evs[2 * k + 1]) for evs in kernel_events for k in range(args.iters)]
     k_ms_local = float(np.mean(kdur))
 
+    # ---- random-gather floor of this shard's SpMV: the same gathers (this shard's own
+    # column indices into the iterate) with nothing else.  The probe and this rank's
+    # plain power-step kernel alternate, so both run at the same clocks (the SpMV is
+    # clock-sensitive and the power cap moves the clock).
+    probe_out = torch.zeros(1, dtype=torch.float64, device=dev)
+    L = lib.load()
+
+    def probe():
+        lib.check(L.tg_gather_probe_f64(pi.indices.data_ptr(), pi.nnz, pi.x[0].data_ptr(), probe_out.data_ptr(),
+                                        stream.cuda_stream), "tg_gather_probe_f64")
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    for _ in range(3):
+        probe()
+    pe, se = [], []
+    for _ in range(10):
+        a, b, c, d = ev(), ev(), ev(), ev()
+        a.record(stream)
+        probe()
+        b.record(stream)
+        c.record(stream)
+        pi._gpu_step(pi.x[0], pi.shard(pi.x[1]))
+        d.record(stream)
+        pe.append((a, b))
+        se.append((c, d))
+    torch.cuda.synchronize(dev)
+    gather_ms_local = float(np.median([a.elapsed_time(b) for a, b in pe]))
+    step_ms_local = float(np.median([c.elapsed_time(d) for c, d in se]))
+
     # ---- e2e through the public API from pinned host buffers
     e2e_ms = []
     for it in range(args.e2e_steps + 1 if args.e2e_steps > 0 else 0):
@@ -793,7 +824,15 @@ def main():
                     if peak_kind == "measured" else "fallback 6.65 TB/s",
                     "kernel": kname, "kernel_ms": round(k_ms, 4),
                     "algorithmic_bytes_per_launch": local_bytes,
-                    "traffic": tr["dram_bytes_per_launch"] if tr else None}
+                    "traffic": tr["dram_bytes_per_launch"] if tr else None,
+                    "gather_floor": {
+                        "ms": round(gather_ms_local, 4),
+                        "gathers_per_s": round(shard.nnz / (gather_ms_local / 1e3), 1),
+                        "step_ms": round(step_ms_local, 4),
+                        "frac": round(gather_ms_local / step_ms_local, 4),
+                        "what": "rank 0: tg_gather_probe_f64 on the shard's own column indices (the "
+                                "SpMV's x gathers alone, same load path and L2 policy) alternated with "
+                                "the plain power-step kernel; frac = probe time / step-kernel time"}}
         line = {
             "metric": "effective_hbm_gbs_power_iteration_spmv",
             "value": round(gbs, 2),

@@ -155,6 +155,13 @@ TG_API int tg_sddmm_f64(const tg_csr* A, const double* U, const double* V, doubl
 TG_API int tg_axpy_f64(const double* x, const double* w, double* z, double alpha, double beta,
                 int64_t n, const tg_sched* s, tg_stream_t stream);
 
+/* Measurement aid (no reference counterpart): *out += sum of x[indices[i]], i < n, with
+ * the SpMV's gather path (same load instruction and L2 policy, four gathers in flight per
+ * thread) and nothing else.  Timing it on a matrix's own column indices gives the
+ * random-gather floor of that matrix's SpMV on this GPU; *out must be zeroed first. */
+TG_API int tg_gather_probe_f64(const int64_t* indices, int64_t n, const double* x, double* out,
+                               tg_stream_t stream);
+
 /* ------------------------------------------------------ power iteration (new) */
 /* Iterated SpMV x <- A x / ||A x||, one process per GPU, rows split into `nparts`
  * contiguous shards.  No counterpart in the reference (north_star's multi-GPU mode).

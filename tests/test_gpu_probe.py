@@ -1,0 +1,33 @@
+"""The gather-floor probe (tg_gather_probe_f64) gathers exactly the SpMV's x values."""
+
+from __future__ import annotations
+
+import pytest
+
+from tilegen_b200 import lib
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [0, 1, 1000, 1 << 20])
+def test_gather_probe_sums_the_gathered_values(n):
+    import torch
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    x = torch.rand(1 << 16, dtype=torch.float64, device=dev, generator=g)
+    idx = torch.randint(0, x.numel(), (n,), device=dev, generator=g, dtype=torch.int64)
+    out = torch.zeros(1, dtype=torch.float64, device=dev)
+    L = lib.load()
+    lib.check(L.tg_gather_probe_f64(idx.data_ptr(), n, x.data_ptr(), out.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream), "tg_gather_probe_f64")
+    torch.cuda.synchronize()
+    ref = float(x[idx].sum()) if n else 0.0
+    assert abs(float(out.item()) - ref) <= 1e-9 * max(1.0, abs(ref))
+
+
+def test_gather_probe_rejects_bad_arguments():
+    L = lib.load()
+    assert L.tg_gather_probe_f64(None, -1, None, None, None) == lib.TG_EINVAL
+    assert L.tg_gather_probe_f64(None, 5, None, None, None) == lib.TG_EINVAL
+    assert L.tg_gather_probe_f64(None, 0, None, None, None) == lib.TG_OK

@@ -1,0 +1,50 @@
+// tg_gather_probe_f64: the random-gather floor of a CSR SpMV, measured on the device.
+//
+// A CSR SpMV over uniformly scattered columns is bound by how fast the SMs can gather
+// 8-byte x values from random addresses (one 32-byte L2 sector per gather), not by the
+// HBM stream of indices and values.  This kernel performs the same gathers as the SpMV
+// -- the same column indices, the same load instruction and L2 policy (ld.global.nc
+// with evict_last), four gathers in flight per thread -- and nothing else (no values,
+// no row offsets, no row reductions, no output vector), so the time it takes is the
+// floor for the SpMV's gather traffic on this GPU.  Benchmarks report the SpMV's time
+// against it next to the HBM roofline.
+#include <algorithm>
+
+#include "tg_common.cuh"
+
+namespace tg {
+namespace {
+
+__global__ void __launch_bounds__(256) gather_probe_kernel(const int64_t* __restrict__ idx, int64_t n,
+                                                           const double* __restrict__ x, double* out) {
+    const uint64_t ps = policy_evict_first();
+    const uint64_t pg = policy_evict_last();
+    const int64_t T = (int64_t)gridDim.x * blockDim.x;
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    double acc = 0.0;
+    for (; i + 3 * T < n; i += 4 * T) {
+        const int64_t c0 = ld_stream(idx + i, ps), c1 = ld_stream(idx + i + T, ps);
+        const int64_t c2 = ld_stream(idx + i + 2 * T, ps), c3 = ld_stream(idx + i + 3 * T, ps);
+        const double g0 = ld_gather(x + c0, pg), g1 = ld_gather(x + c1, pg);
+        const double g2 = ld_gather(x + c2, pg), g3 = ld_gather(x + c3, pg);
+        acc += (g0 + g1) + (g2 + g3);
+    }
+    for (; i < n; i += T) acc += ld_gather(x + ld_stream(idx + i, ps), pg);
+    acc = group_sum<kWarp>(acc, kFull);
+    if ((threadIdx.x % kWarp) == 0) atomicAdd(out, acc);
+}
+
+}  // namespace
+}  // namespace tg
+
+using namespace tg;
+
+extern "C" int tg_gather_probe_f64(const int64_t* indices, int64_t n, const double* x, double* out,
+                                   tg_stream_t stream) {
+    if (n < 0) return set_error(TG_EINVAL, "tg_gather_probe_f64: negative n");
+    if (n > 0 && (!indices || !x || !out)) return set_error(TG_EINVAL, "tg_gather_probe_f64: null pointer argument");
+    if (n == 0) return TG_OK;
+    const int64_t blocks = std::min<int64_t>(ceil_div(n, 256 * 4), 148 * 16);
+    gather_probe_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(indices, n, x, out);
+    return check_launch("gather_probe_kernel");
+}
