@@ -171,6 +171,12 @@ TG_API int tg_gather_probe_f64(const int64_t* indices, int64_t n, const double* 
  * (j -> owner(j) * stride + j - first_row(owner)).  The workspace must be zero-filled
  * before its first use; every call leaves it zeroed. */
 TG_API size_t tg_power_workspace_bytes(int64_t nnz, const tg_sched* s);
+/* out[i] = owner(j) * stride + (j - bounds[owner(j)]) for j = indices[i], i < nnz: the
+ * column renumbering above, on the device.  `bounds` (host memory, nparts + 1 <= 65
+ * entries) are the row bounds of the shards, bounds[0] = 0, each shard shorter than
+ * `stride`; the indices must lie in [0, bounds[nparts]).  out may equal indices. */
+TG_API int tg_renumber_columns(const int64_t* indices, int64_t* out, int64_t nnz, const int64_t* bounds,
+                               int32_t nparts, int64_t stride, tg_stream_t stream);
 /* y[0..rows) = A x / sqrt(sum of the nparts slots of x); y[stride-1] = sum(y^2). */
 TG_API int tg_power_step_f64(const tg_csr* A, const double* x, int32_t nparts, int64_t stride,
                              double* y, const tg_sched* s, void* workspace,

@@ -6,6 +6,7 @@ from __future__ import annotations
 import ctypes
 import subprocess
 
+import numpy as np
 import pytest
 
 from tilegen_b200 import lib
@@ -17,7 +18,7 @@ def test_library_loads_and_reports_version():
 
 def test_every_header_symbol_is_exported_and_typed():
     declared = set(lib.header_symbols())
-    assert len(declared) == 38
+    assert len(declared) == 39
     assert declared == set(lib.SIGNATURES)
     out = subprocess.run(["nm", "-D", "--defined-only", lib.lib_path()], capture_output=True, text=True).stdout
     exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
@@ -97,3 +98,13 @@ def test_null_arguments_fail_without_touching_the_device():
     bad = lib.TgCsr(-1, 4, 0, 0, 0, 0)
     assert L.tg_spmv_f64(ctypes.byref(bad), None, None, ctypes.byref(s), None, 0, None) == lib.TG_EINVAL
     assert "negative size" in lib.last_error()
+
+
+def test_renumber_columns_rejects_bad_bounds():
+    L = lib.load()
+    b = np.array([0, 10, 5], dtype=np.int64)  # decreasing
+    assert L.tg_renumber_columns(None, None, 0, b.ctypes.data, 2, 32, None) == lib.TG_EINVAL
+    b = np.array([0, 40], dtype=np.int64)  # shard longer than the stride allows
+    assert L.tg_renumber_columns(None, None, 0, b.ctypes.data, 1, 32, None) == lib.TG_EINVAL
+    b = np.array([0, 20], dtype=np.int64)
+    assert L.tg_renumber_columns(None, None, 0, b.ctypes.data, 1, 32, None) == lib.TG_OK

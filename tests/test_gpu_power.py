@@ -150,3 +150,23 @@ def test_p2p_fused_step_emulated_on_one_gpu(parts):
     xr, nr = O.power_iteration(A, x0, iters)
     assert rel(x, xr) <= 1e-9
     assert abs(float(pis[0].result()[1]) - nr) <= 1e-9 * nr
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("parts", [1, 3, 8])
+def test_renumber_columns_kernel_matches_host(parts):
+    """tg_renumber_columns (device) gives the host restatement's renumbering."""
+    import torch
+
+    from tilegen_b200.power import nnz_balanced_bounds, padded_stride, renumber_columns
+
+    rng = np.random.default_rng(parts)
+    n = 10007
+    row_nnz = rng.integers(0, 9, size=n)
+    bounds = nnz_balanced_bounds(row_nnz, parts)
+    stride = padded_stride(bounds)
+    j = rng.integers(0, n, size=50001).astype(np.int64)
+    want = renumber_columns(j, bounds, stride)
+    got = renumber_columns(torch.as_tensor(j, device="cuda"), bounds, stride).cpu().numpy()
+    assert np.array_equal(got, want)
+

@@ -1,0 +1,57 @@
+// tg_renumber_columns: column renumbering of a row shard to the padded iterate layout of
+// the power iteration (the device half of the nnz-balanced partitioner).
+//
+// With the rows split at bounds[0] = 0 < bounds[1] < ... < bounds[P] = N and every shard
+// stored at a stride of `stride` doubles, column j (owned by shard q: bounds[q] <= j <
+// bounds[q+1]) moves to q * stride + (j - bounds[q]).  One streaming pass, HBM-bound
+// (16 bytes per nonzero); the bounds travel in the kernel parameters.
+#include <algorithm>
+
+#include "tg_common.cuh"
+
+namespace tg {
+namespace {
+
+constexpr int kMaxParts = 64;
+
+struct Bounds {
+    int64_t b[kMaxParts + 1];
+    int parts;
+};
+
+__global__ void __launch_bounds__(256) renumber_kernel(const int64_t* __restrict__ in, int64_t* out, int64_t n,
+                                                       const Bounds bd, int64_t stride) {
+    const uint64_t ps = policy_evict_first();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = ld_stream(in + i, ps);
+        int q = 0;
+        while (q + 1 < bd.parts && j >= bd.b[q + 1]) ++q;  // parts <= 64: a short scan
+        out[i] = (int64_t)q * stride + (j - bd.b[q]);
+    }
+}
+
+}  // namespace
+}  // namespace tg
+
+using namespace tg;
+
+extern "C" int tg_renumber_columns(const int64_t* indices, int64_t* out, int64_t nnz, const int64_t* bounds,
+                                   int32_t nparts, int64_t stride, tg_stream_t stream) {
+    if (nnz < 0 || nparts < 1 || nparts > kMaxParts || stride < 1)
+        return set_error(TG_EINVAL, "tg_renumber_columns: bad arguments (nnz=%lld nparts=%d stride=%lld)",
+                         (long long)nnz, nparts, (long long)stride);
+    if (!bounds || (nnz > 0 && (!indices || !out)))
+        return set_error(TG_EINVAL, "tg_renumber_columns: null pointer argument");
+    Bounds bd{};
+    bd.parts = nparts;
+    for (int q = 0; q <= nparts; ++q) {
+        bd.b[q] = bounds[q];
+        if (q > 0 && (bd.b[q] < bd.b[q - 1] || bd.b[q] - bd.b[q - 1] > stride - 1))
+            return set_error(TG_EINVAL, "tg_renumber_columns: bounds must be non-decreasing with shards < stride");
+    }
+    if (bd.b[0] != 0) return set_error(TG_EINVAL, "tg_renumber_columns: bounds[0] must be 0");
+    if (nnz == 0) return TG_OK;
+    const int64_t blocks = std::min<int64_t>(ceil_div(nnz, 256), 148 * 16);
+    renumber_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(indices, out, nnz, bd, stride);
+    return check_launch("renumber_kernel");
+}

@@ -96,6 +96,8 @@ SIGNATURES = {
     "tg_last_error_string": (ctypes.c_char_p, []),
     "tg_last_status": (ctypes.c_int, []),
     "tg_launch_count": (ctypes.c_uint64, []),
+    "tg_renumber_columns": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                           ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p]),
     "tg_gather_probe_f64": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p]),
     "tg_default_schedule": (None, [_SP]),

@@ -52,14 +52,26 @@ def padded_stride(bounds: np.ndarray, align: int = 32) -> int:
 
 
 def renumber_columns(indices, bounds, stride: int):
-    """j -> owner(j) * stride + (j - bounds[owner(j)]), on numpy or torch tensors."""
+    """j -> owner(j) * stride + (j - bounds[owner(j)]).  CUDA tensors go through the
+    library's kernel (tg_renumber_columns, on the current stream); numpy arrays and CPU
+    tensors are renumbered on the host (the gloo tests)."""
     try:
         import torch
 
         if isinstance(indices, torch.Tensor):
-            b = torch.as_tensor(bounds, dtype=torch.int64, device=indices.device)
-            owner = torch.searchsorted(b, indices, right=True) - 1
-            return owner * stride + (indices - b[owner])
+            if indices.is_cuda:
+                from . import lib as _lib
+
+                L = _lib.load()
+                idx = indices.contiguous().to(torch.int64)
+                out = torch.empty_like(idx)
+                b = np.ascontiguousarray(bounds, dtype=np.int64)
+                with torch.cuda.device(idx.device):
+                    st = torch.cuda.current_stream(idx.device).cuda_stream
+                    _lib.check(L.tg_renumber_columns(idx.data_ptr(), out.data_ptr(), idx.numel(), b.ctypes.data,
+                                                     b.size - 1, int(stride), st), "tg_renumber_columns")
+                return out
+            return torch.from_numpy(renumber_columns(indices.numpy(), bounds, stride))
     except ImportError:  # pragma: no cover
         pass
     b = np.asarray(bounds, dtype=np.int64)
