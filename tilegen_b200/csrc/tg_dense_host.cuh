@@ -36,8 +36,21 @@ inline int pow2_ceil(int64_t v) {
 
 inline bool aligned_to(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Default merge chunk: 256 nonzeros per lane group.  SDDMM has no row sums to split, so
+// small chunks cost it nothing: its chunk is halved (down to 32) until the call has at
+// least 32768 chunks, so that a small matrix (or one GPU's shard of a large one) still
+// fills every SM with groups.  SpMM keeps 256: each chunk boundary inside a row costs a
+// K-wide partial and its fix-up.  A function of nnz and the op alone, so that the
+// workspace size and the launch agree.
+inline int64_t default_dense_chunk(int64_t nnz, bool is_spmm) {
+    int64_t S = 256;
+    if (!is_spmm)
+        while (S > 32 && nnz / S < 32768) S /= 2;
+    return S;
+}
+
 template <typename T>
-DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void* p0, const void* p1) {
+DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void* p0, const void* p1, int64_t nnz) {
     DenseChoice d{};
     const int vmax = sizeof(T) == 4 ? 4 : 2;
     int vec = std::min(std::max(s.vector_width, 1), vmax);
@@ -55,7 +68,7 @@ DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void*
     d.U = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
     d.block = (s.block_size >= 512) ? 512 : (s.block_size >= 256 ? 256 : 128);
     d.merge = (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM);
-    d.S = s.chunk_nnz > 0 ? s.chunk_nnz : 256;
+    d.S = s.chunk_nnz > 0 ? s.chunk_nnz : default_dense_chunk(nnz, is_spmm);
     return d;
 }
 
@@ -128,7 +141,7 @@ size_t dense_ws_bytes(int64_t rows, int64_t nnz, int64_t K, const tg_sched& s, b
     (void)rows;
     if ((s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_STREAM) || nnz <= 0 || K <= 0) return 0;
     // alignment does not change the partial width's upper bound: size for the widest tile
-    const DenseChoice d = choose_dense<T>(s, K, is_spmm, nullptr, nullptr);
+    const DenseChoice d = choose_dense<T>(s, K, is_spmm, nullptr, nullptr, nnz);
     const int64_t nchunks = ceil_div(nnz, d.S);
     const int64_t width = is_spmm ? (int64_t)d.G * (sizeof(T) == 4 ? 4 : 2) * 4 : 0;
     return split_ws_bytes(nchunks, width, sizeof(T));
@@ -140,7 +153,7 @@ int dense_run(bool is_spmm, const tg_csr& A, const T* B, const T* U, T* C, int64
               size_t ws_bytes, cudaStream_t st) {
     if (K <= 0) return set_error(TG_EINVAL, "dense width K must be positive (got %lld)", (long long)K);
     if (A.rows == 0) return TG_OK;
-    const DenseChoice d = choose_dense<T>(s, K, is_spmm, B, is_spmm ? (const void*)C : (const void*)U);
+    const DenseChoice d = choose_dense<T>(s, K, is_spmm, B, is_spmm ? (const void*)C : (const void*)U, A.nnz);
     DenseArgs<T> a{};
     a.indptr = A.indptr;
     a.indices = A.indices;
