@@ -43,7 +43,6 @@ struct SpmvArgs {
     T* head;
     T* tail;
     uint32_t* err;
-    int use_bulk;
 };
 
 template <typename T, int TPR, int U, int V, bool AXPY>
@@ -341,7 +340,6 @@ int spmv_run(const tg_csr& A, const T* x, T* y, const Epi<T, AXPY>& epi, const t
         a.head = static_cast<T*>(w.head);
         a.tail = static_cast<T*>(w.tail);
         a.err = w.err;
-        a.use_bulk = aligned16(A.indices) && aligned16(A.data);
         if (nchunks > 0x7fffffff) return set_error(TG_EINVAL, "too many chunks (%lld)", (long long)nchunks);
         // programmatic launch: the chunk staging of the merge kernel overlaps the partition
         cudaLaunchConfig_t cfg = {};
