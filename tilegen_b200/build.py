@@ -89,7 +89,23 @@ def build(force: bool = False, jobs: int = 0, verbose: bool = False) -> str:
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError("link failed:\n%s%s" % (res.stdout, res.stderr))
+    build_cli(nvcc, force)
     return LIB_PATH
+
+
+CLI_SRC = os.path.join(PKG_DIR, "cli", "tilegen_b200_bench.cpp")
+CLI_PATH = os.path.join(PKG_DIR, "tilegen_b200_bench")
+
+
+def build_cli(nvcc: str, force: bool = False) -> str:
+    """The C++ bench harness (the b200 counterpart of the reference's tilegen_bench): host
+    code only; it dlopen()s the library at run time."""
+    if force or _stale(CLI_PATH, [CLI_SRC, *_headers()]):
+        cmd = [nvcc, "-O2", "-std=c++17", "-o", CLI_PATH, CLI_SRC, "-ldl"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError("bench harness build failed:\n%s%s" % (res.stdout, res.stderr))
+    return CLI_PATH
 
 
 def main(argv=None) -> int:
