@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run in the build container, where the reference tree is mounted (default
-/root/reference, override with TILEGEN_REFERENCE_ROOT):
+Run where the reference tree is checked out (its location is taken from
+TILEGEN_REFERENCE_ROOT, with the build container's mount point as the default):
 
     python tests/golden/make_golden.py
 
