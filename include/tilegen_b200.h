@@ -235,6 +235,33 @@ TG_API int tg_ipc_close(void* ptr);
 TG_API int tg_spmv_f64_noalloc(const tg_csr* A, const double* x, double* y, const tg_sched* s,
                                tg_stream_t stream);
 
+/* ------------------------------------------------- multi-GPU, one process (new) */
+/* One process driving `nranks` GPUs of a node (no counterpart in the reference; the
+ * multi-GPU mode of north_star).  tg_dist_init creates a stream per GPU and enables peer
+ * access between every pair (TG_EUNSUPPORTED when a pair cannot map each other's
+ * memory); one rank per GPU, each device listed once, at most 8.  The calls take HOST
+ * CSR matrices and host dense operands, split the rows into nnz-balanced contiguous
+ * shards, replicate the dense inputs, run every shard on its GPU and gather the output
+ * rows to the host.  timeout_s > 0 is a host deadline: past it the call returns
+ * TG_ETIMEDOUT, after the device work (whose own waits are bounded) has stopped.
+ * The caller's current device is left unchanged. */
+typedef struct tg_dist tg_dist;
+TG_API int tg_dist_init(int32_t nranks, const int32_t* devices, tg_dist** out);
+/* Waits for the context's work and releases it (NULL is accepted). */
+TG_API int tg_dist_finalize(tg_dist* d);
+/* `iters` power iterations x <- A x / ||A x|| of a square fp64 matrix from x0 (host, A.cols
+ * values, any scale) with the fused step + peer-memory exchange; x_out (host, A.rows)
+ * receives the final iterate, *lambda the norm of the last A x (x0 normalised and its
+ * norm when iters = 0).  A peer that stops answering ends the call with TG_ETIMEDOUT. */
+TG_API int tg_dist_spmv_power(tg_dist* d, const tg_csr* A, const double* x0, int32_t iters, const tg_sched* s,
+                              double* x_out, double* lambda, double timeout_s);
+/* C (host, A.rows x k) = A B with A's values fp32 and B (host, A.cols x k) fp32. */
+TG_API int tg_dist_spmm_f32(tg_dist* d, const tg_csr* A, const float* B, int64_t k, float* C, const tg_sched* s,
+                            double timeout_s);
+/* out (host, A.nnz, A's order) = A .* (U V^T) on A's pattern; U (A.rows x k), V (A.cols x k). */
+TG_API int tg_dist_sddmm_f32(tg_dist* d, const tg_csr* A, const float* U, const float* V, int64_t k, float* out,
+                             const tg_sched* s, double timeout_s);
+
 /* --------------------------------------------- reference-compatible launchers */
 /* Signatures as emitted by tilegen/codegen.py:_abi (226-280) for the standard kernels
  * of tilegen/dsl.py:214-256; argument order/meaning as in tilegen/verify.py:166-173. */

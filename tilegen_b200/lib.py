@@ -96,6 +96,14 @@ SIGNATURES = {
     "tg_last_error_string": (ctypes.c_char_p, []),
     "tg_last_status": (ctypes.c_int, []),
     "tg_launch_count": (ctypes.c_uint64, []),
+    "tg_dist_init": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_void_p)]),
+    "tg_dist_finalize": (ctypes.c_int, [ctypes.c_void_p]),
+    "tg_dist_spmv_power": (ctypes.c_int, [ctypes.c_void_p, _CP, ctypes.c_void_p, ctypes.c_int32, _SP, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_double]),
+    "tg_dist_spmm_f32": (ctypes.c_int, [ctypes.c_void_p, _CP, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, _SP,
+                                        ctypes.c_double]),
+    "tg_dist_sddmm_f32": (ctypes.c_int, [ctypes.c_void_p, _CP, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                         ctypes.c_void_p, _SP, ctypes.c_double]),
     "tg_renumber_columns": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                            ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p]),
     "tg_gather_probe_f64": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
