@@ -858,6 +858,15 @@ def main():
                          "block": args.block},
             "lambda": float(h_lam[0]),
         }
+        if world > 1:
+            # communication broken out per iteration: the timed iteration (with its
+            # exchange, max over ranks) against rank 0's compute-only step kernel timed
+            # beside the gather probe, and the iterate bytes rank 0 receives
+            it_ms = ms_step / args.iters
+            line["comm"] = {"iteration_ms": round(it_ms, 4), "compute_only_ms": round(step_ms_local, 4),
+                            "exchange_ms": round(max(it_ms - step_ms_local, 0.0), 4),
+                            "received_bytes_per_iteration": int(8 * (n - (r1 - r0))),
+                            "exchange": args.exchange}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(shard, x0_all)
         print(json.dumps(line), flush=True)
