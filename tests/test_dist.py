@@ -38,6 +38,12 @@ def test_dist_init_rejects_bad_arguments():
     assert "twice" in lib.last_error()
     assert L.tg_dist_init(1, (ctypes.c_int32 * 1)(0), None) == lib.TG_EINVAL
     assert L.tg_dist_finalize(None) == lib.TG_OK
+    m = M.edge_matrix()
+    A = _host_csr(m, m.data)
+    lam = ctypes.c_double()
+    assert L.tg_dist_spmv_power(None, ctypes.byref(A), None, 1, None, None, ctypes.byref(lam), 0.0) == lib.TG_EINVAL
+    assert L.tg_dist_spmm_f32(None, ctypes.byref(A), None, 8, None, None, 0.0) == lib.TG_EINVAL
+    assert L.tg_dist_sddmm_f32(None, ctypes.byref(A), None, None, 8, None, None, 0.0) == lib.TG_EINVAL
 
 
 def _devices(n):
