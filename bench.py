@@ -856,7 +856,7 @@ def main():
             "wall_s_timed": round(wall, 4),
             "schedule": {"split": args.split, "tpr": args.tpr, "unroll": args.unroll, "vec": args.vec,
                          "block": args.block},
-            "lambda": float(h_lam[0]),
+            "lambda": float(lam[0].item()),  # the timed steps' result (rank 0's copy)
         }
         if world > 1:
             # communication broken out per iteration: the timed iteration (with its
