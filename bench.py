@@ -12,7 +12,14 @@ Metric: effective HBM GB/s = compulsory SpMV bytes (8(M+1) + 16 nnz + 8 N + 8 M 
 whole matrix) x 20 iterations / step time, whole job, max over ranks.  `value` has A and
 x0 resident in HBM; `e2e` repeats the step through the public API from pinned host
 buffers (H2D of the shard, column renumbering, 20 iterations, D2H of x and lambda).
-The inputs (4.29 GB) exceed the 126 MB L2, so no flush is needed between steps.
+The inputs (4.29 GB) exceed the 126 MB L2, so no flush is needed between steps.  On one
+GPU the line also carries `cusparse` (cuSPARSE SpMV on the same arrays).
+
+The same line carries `workloads`: the other BASELINE configurations (C1 uniform, C2
+banded, C3 power-law SpMV; C5 SpMM K=128 and SDDMM K=64), each row-sharded over the same
+ranks and timed the same way (L2 flushed before each call where the problem fits in L2),
+with ms, effective GB/s, roofline fraction, cuSPARSE and the reference's CPU kernel
+beside it.  `--workload c1|c2|c3|c5-spmm|c5-sddmm` prints one of them as its own line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 """
@@ -74,6 +81,8 @@ def parse():
     ap.add_argument("--block", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="c4: skip the C1-C3 / C5 measurements that the default line carries in `workloads`")
     args = ap.parse_args()
     d = SCHEDULES[args.workload]
     for k in ("split", "tpr", "unroll", "vec", "block"):
@@ -435,30 +444,29 @@ def run_matrix_reference(args, rank: int, world: int):
     return 0
 
 
-def run_matrix_workload(args, rank: int, world: int, local_rank: int):
-    """C1-C3 (one SpMV per step) and C5 (one SpMM or SDDMM per step), row-sharded over the
-    ranks with the dense operands replicated (strong scaling, no communication)."""
+def make_sched(split: str, tpr: int, unroll: int, vec: int, block: int):
+    from tilegen_b200 import lib
+
+    sch = lib.default_schedule()
+    sch.threads_per_row, sch.unroll, sch.vector_width, sch.block_size, sch.tile = tpr, unroll, vec, block, 32
+    sch.split = {"rowwise": lib.TG_SPLIT_ROWWISE, "merge": lib.TG_SPLIT_MERGE, "stream": lib.TG_SPLIT_STREAM}[split]
+    lib.validate_schedule(sch)
+    return sch
+
+
+def measure_matrix(wl: str, sched: dict, steps: int, warmup: int, rank: int, world: int, dev, barrier,
+                   e2e_steps: int, want_cpu: bool, want_cusparse: bool, sample_clocks: bool):
+    """One C1-C3 / C5 workload: rank `rank`'s row shard (nnz-balanced, dense operands
+    replicated), `steps` timed calls after `warmup`, L2 flushed before each call when the
+    problem fits in L2.  Returns the measurement record (times are this rank's; the
+    caller takes the max over ranks)."""
     import torch
-    import torch.distributed as dist
 
     from tilegen_b200 import device as D
     from tilegen_b200 import lib, matrices as Mx
     from tilegen_b200.power import nnz_balanced_bounds
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
     L = lib.load()
-    wl = args.workload
     kernel = matrix_kernel(wl)
     c5 = wl.startswith("c5")
     A = Mx.baseline_matrix("c5" if c5 else wl)
@@ -468,12 +476,7 @@ def run_matrix_workload(args, rank: int, world: int, local_rank: int):
     S = row_shard(A, r0, r1)
     dt = torch.float32 if c5 else torch.float64
     Ad = D.DeviceCSR.from_host(S, dev, dt)
-
-    sch = lib.default_schedule()
-    sch.threads_per_row, sch.unroll, sch.vector_width, sch.block_size, sch.tile = (args.tpr, args.unroll, args.vec,
-                                                                                   args.block, 32)
-    sch.split = {"rowwise": lib.TG_SPLIT_ROWWISE, "merge": lib.TG_SPLIT_MERGE, "stream": lib.TG_SPLIT_STREAM}[args.split]
-    lib.validate_schedule(sch)
+    sch = make_sched(sched["split"], sched["tpr"], sched["unroll"], sched["vec"], sched["block"])
 
     # pinned host inputs (e2e) and their device copies
     h_in = {k: torch.from_numpy(np.ascontiguousarray(v[r0:r1] if k == "U" else v)).pin_memory()
@@ -493,17 +496,17 @@ def run_matrix_workload(args, rank: int, world: int, local_rank: int):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if flush_needed else None
     stream = torch.cuda.current_stream(dev)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     barrier()
-    sampler = ClockSampler(local_rank) if rank == 0 else None
+    sampler = ClockSampler(dev.index) if sample_clocks else None
     if sampler:
         sampler.start()
     barrier()
     n0 = L.tg_launch_count()
     evs = []
     wall0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         if flush is not None:
             flush.zero_()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -521,7 +524,7 @@ def run_matrix_workload(args, rank: int, world: int, local_rank: int):
     # e2e through the public API: H2D of the step's dense inputs from pinned memory, the
     # call, D2H of the output shard
     e2e = []
-    for it in range(args.e2e_steps + 1 if args.e2e_steps > 0 else 0):
+    for it in range(e2e_steps + 1 if e2e_steps > 0 else 0):
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -534,24 +537,86 @@ def run_matrix_workload(args, rank: int, world: int, local_rank: int):
         barrier()
         if it > 0:
             e2e.append(e0.elapsed_time(e1))
-    e2e_local = float(np.mean(e2e)) if e2e else float("nan")
+    rec = {"wl": wl, "A": A, "S": S, "kernel": kernel, "ms_local": ms_local,
+           "e2e_local": float(np.mean(e2e)) if e2e else float("nan"), "launches": int(launches), "clocks": clocks,
+           "wall": wall, "flush": flush is not None, "c5": c5, "inputs": inputs, "schedule": dict(sched),
+           "h2d": int(sum(v.numel() * v.element_size() for v in h_in.values())),
+           "d2h": int(h_out.numel() * h_out.element_size())}
+    if want_cusparse:
+        rec["cusparse"] = cusparse_compare(wl, Ad, d_in, flush, steps, matrix_bytes(wl, A))
+    if want_cpu:
+        reps = 3 if c5 else 20
+        sec, kind, desc, threads = cpu_matrix_sample(wl, A, inputs, reps)
+        if sec is not None:
+            rec["cpu_baseline"] = {"value": round(matrix_bytes(wl, A) / sec / 1e9, 3), "unit": "GB/s",
+                                   "cores": threads, "kind": kind,
+                                   "sample": "%d whole-matrix calls on the host cores" % reps, "impl": desc}
+    return rec
 
-    vals = torch.tensor([ms_local, e2e_local], dtype=torch.float64, device=dev)
+
+def matrix_kernel_name(kernel: str, split: str) -> str:
+    return {"spmv": "spmv_rowwise_kernel" if split == "rowwise" else "spmv_merge_kernel",
+            "spmm": "spmm kernel", "sddmm": "sddmm kernel"}[kernel]
+
+
+def summarise_matrix(rec, ms_step: float, world: int, peak: float):
+    """Compact per-workload record for the default run's `workloads` object."""
+    wl, A, S = rec["wl"], rec["A"], rec["S"]
+    total = matrix_bytes(wl, A)
+    local = matrix_bytes(wl, S)
+    achieved = local / (rec["ms_local"] / 1e3) / 1e9
+    d = {"workload": matrix_config(wl, A, world, rec["flush"])["workload"], "rows": A.rows, "nnz": A.nnz,
+         "ms": round(ms_step, 5), "value": round(total / (ms_step / 1e3) / 1e9, 2), "unit": "GB/s",
+         "gflops": round(matrix_flops(wl, A) / (ms_step / 1e3) / 1e9, 2),
+         "roofline_frac": round(achieved / peak, 4), "algorithmic_bytes": int(total),
+         "l2": "flushed before every call" if rec["flush"] else "inputs larger than L2",
+         "schedule": rec["schedule"], "gpu_launches": rec["launches"]}
+    if "cusparse" in rec:
+        c = rec["cusparse"]
+        d["cusparse"] = c
+        if "ms_per_step" in c:
+            d["vs_cusparse"] = round(c["ms_per_step"] / ms_step, 3)
+    if "cpu_baseline" in rec:
+        d["cpu_baseline"] = rec["cpu_baseline"]
+    return d
+
+
+def run_matrix_workload(args, rank: int, world: int, local_rank: int):
+    """C1-C3 (one SpMV per step) and C5 (one SpMM or SDDMM per step), row-sharded over the
+    ranks with the dense operands replicated (strong scaling, no communication)."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    wl = args.workload
+    sched = {"split": args.split, "tpr": args.tpr, "unroll": args.unroll, "vec": args.vec, "block": args.block}
+    rec = measure_matrix(wl, sched, args.steps, args.warmup, rank, world, dev, barrier, args.e2e_steps,
+                         want_cpu=(world == 1 and rank == 0 and not args.no_cpu_baseline),
+                         want_cusparse=(world == 1 and not args.no_cusparse), sample_clocks=(rank == 0))
+    vals = torch.tensor([rec["ms_local"], rec["e2e_local"]], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     ms_step, e2e_ms = [float(v) for v in vals.cpu()]
+    A, S, kernel = rec["A"], rec["S"], rec["kernel"]
     total = matrix_bytes(wl, A)
     gbs = total / (ms_step / 1e3) / 1e9
-
-    line = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
         local_bytes = matrix_bytes(wl, S)  # this rank's rows, the whole replicated dense input
-        achieved = local_bytes / (ms_local / 1e3) / 1e9
-        kname = {"spmv": "spmv_rowwise_kernel" if args.split == "rowwise" else "spmv_merge_kernel",
-                 "spmm": "spmm kernel", "sddmm": "sddmm kernel"}[kernel]
+        achieved = local_bytes / (rec["ms_local"] / 1e3) / 1e9
+        kname = matrix_kernel_name(kernel, args.split)
         tr = traffic_record("%s_%d" % (wl, world), kname)
-        h2d = int(sum(v.numel() * v.element_size() for v in h_in.values()))
         line = {
             "metric": "effective_hbm_gbs_" + kernel,
             "value": round(gbs, 2),
@@ -563,36 +628,28 @@ def run_matrix_workload(args, rank: int, world: int, local_rank: int):
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "f32" if c5 else "f64",
+            "dtype": "f32" if rec["c5"] else "f64",
             "data": "synthetic (seeded generators, values U(-1,1))",
-            "config": matrix_config(wl, A, world, flush is not None),
+            "config": matrix_config(wl, A, world, rec["flush"]),
             "gflops": round(matrix_flops(wl, A) / (ms_step / 1e3) / 1e9, 2),
-            "e2e": {"value": round(total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": int(h_out.numel() * h_out.element_size()), "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": int(launches),
+            "e2e": {"value": round(total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": rec["h2d"],
+                    "d2h_bytes_per_step": rec["d2h"], "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": rec["launches"],
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
                          "peak_source": (peak_kind + " (MEASURED_PEAKS.json hbm_gbs)") if peak_kind == "measured"
                          else "fallback 6.65 TB/s",
                          "kernel": kname + " (whole call, every launch of the step)",
-                         "kernel_ms": round(ms_local, 5), "algorithmic_bytes_per_launch": int(local_bytes),
+                         "kernel_ms": round(rec["ms_local"], 5), "algorithmic_bytes_per_launch": int(local_bytes),
                          "traffic": tr["dram_bytes_per_launch"] if tr else None},
-            "clocks": clocks,
-            "wall_s_timed": round(wall, 4),
-            "schedule": {"split": args.split, "tpr": args.tpr, "unroll": args.unroll, "vec": args.vec,
-                         "block": args.block},
+            "clocks": rec["clocks"],
+            "wall_s_timed": round(rec["wall"], 4),
+            "schedule": rec["schedule"],
         }
-        if world == 1 and not args.no_cusparse:
-            line["cusparse"] = cusparse_compare(wl, Ad, d_in, flush, args.steps, total)
-    barrier()
-    if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
-            sec, kind, desc, threads = cpu_matrix_sample(wl, A, inputs, 3 if c5 else 20)
-            if sec is not None:
-                cg = matrix_bytes(wl, A) / sec / 1e9
-                line["cpu_baseline"] = {"value": round(cg, 3), "unit": "GB/s", "cores": threads, "kind": kind,
-                                        "sample": "%d whole-matrix calls on the host cores" % (3 if c5 else 20),
-                                        "impl": desc}
+        if "cusparse" in rec:
+            line["cusparse"] = rec["cusparse"]
+        if "cpu_baseline" in rec:
+            line["cpu_baseline"] = rec["cpu_baseline"]
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -748,12 +805,13 @@ def main():
     # column indices into the iterate) with nothing else.  The probe and this rank's
     # plain power-step kernel alternate, so both run at the same clocks (the SpMV is
     # clock-sensitive and the power cap moves the clock).
+    from tilegen_b200 import bench_probe
+
     probe_out = torch.zeros(1, dtype=torch.float64, device=dev)
-    L = lib.load()
 
     def probe():
-        lib.check(L.tg_gather_probe_f64(pi.indices.data_ptr(), pi.nnz, pi.x[0].data_ptr(), probe_out.data_ptr(),
-                                        stream.cuda_stream), "tg_gather_probe_f64")
+        bench_probe.gather_probe_f64(pi.indices.data_ptr(), pi.nnz, pi.x[0].data_ptr(), probe_out.data_ptr(),
+                                     stream.cuda_stream)
 
     def ev():
         return torch.cuda.Event(enable_timing=True)
@@ -801,6 +859,33 @@ def main():
             e2e_ms.append(e0.elapsed_time(e1))
         del pe, ip, dd, xx
     e2e_local = float(np.mean(e2e_ms)) if e2e_ms else float("nan")
+
+    # ---- cuSPARSE SpMV on the same device arrays (N=1), a comparison only
+    c4_cusparse = None
+    if world == 1 and not args.no_cusparse:
+        c4_cusparse = cusparse_c4(pi, n, dev, spmv_bytes(n, n, shard.nnz))
+
+    # ---- the other BASELINE configurations (C1-C3 SpMV, C5 SpMM / SDDMM), each on its
+    # own matrix, row-sharded over the same ranks
+    workloads = {}
+    if not args.no_workloads:
+        peak, _ = measured_peaks()
+        for wl in ("c1", "c2", "c3", "c5-spmm", "c5-sddmm"):
+            rec = measure_matrix(wl, SCHEDULES[wl], args.steps, args.warmup, rank, world, dev, barrier, 2,
+                                 want_cpu=(world == 1 and rank == 0 and not args.no_cpu_baseline),
+                                 want_cusparse=(world == 1 and not args.no_cusparse), sample_clocks=False)
+            v = torch.tensor([rec["ms_local"], rec["e2e_local"]], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(v, op=dist.ReduceOp.MAX)
+            if rank == 0:
+                d = summarise_matrix(rec, float(v[0].item()), world, peak)
+                e2e_w = float(v[1].item())
+                d["e2e"] = {"value": round(matrix_bytes(wl, rec["A"]) / (e2e_w / 1e3) / 1e9, 2), "unit": "GB/s",
+                            "ms": round(e2e_w, 4), "h2d_bytes_per_step": rec["h2d"],
+                            "d2h_bytes_per_step": rec["d2h"]}
+                workloads[wl] = d
+            del rec
+            torch.cuda.empty_cache()
 
     # ---- max over ranks
     vals = torch.tensor([ms_local, k_ms_local, e2e_local], dtype=torch.float64, device=dev)
@@ -867,13 +952,47 @@ def main():
                             "exchange_ms": round(max(it_ms - step_ms_local, 0.0), 4),
                             "received_bytes_per_iteration": int(8 * (n - (r1 - r0))),
                             "exchange": args.exchange}
+        if c4_cusparse is not None:
+            c4_cusparse["vs_cusparse"] = (round(c4_cusparse["ms_per_spmv"] / k_ms, 3)
+                                          if "ms_per_spmv" in c4_cusparse else None)
+            line["cusparse"] = c4_cusparse
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(shard, x0_all)
+        if workloads:
+            line["workloads"] = workloads
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def cusparse_c4(pi, n: int, dev, nbytes: int, reps: int = 10):
+    """cuSPARSE SpMV (torch.mv on a CSR tensor) on the power iteration's own arrays (one
+    GPU: the padded layout is the identity), timed per call with CUDA events; compared
+    with the fused power-step kernel, which does the SpMV plus the norm."""
+    import torch
+
+    try:
+        Sp = torch.sparse_csr_tensor(pi.indptr, pi.indices, pi.data, size=(n, n))
+        x = pi.x[0][:n].clone()
+        for _ in range(3):
+            torch.mv(Sp, x)
+        torch.cuda.synchronize(dev)
+        ts = []
+        for _ in range(reps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            torch.mv(Sp, x)
+            b.record()
+            ts.append((a, b))
+        torch.cuda.synchronize(dev)
+        ms = float(np.mean([a.elapsed_time(b) for a, b in ts]))
+        return {"op": "torch.mv on a CSR tensor (cusparseSpMV), same arrays, inputs larger than L2",
+                "ms_per_spmv": round(ms, 4), "value": round(nbytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s"}
+    except Exception as exc:  # noqa: BLE001 -- a comparison must not fail the bench
+        return {"error": str(exc)[:200]}
 
 
 def cpu_baseline(A, x0):

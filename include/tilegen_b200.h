@@ -136,6 +136,11 @@ TG_API int tg_spmv_f32(const tg_csr* A, const float* x, float* y, const tg_sched
 TG_API int tg_fused_spmv_axpy_f64(const tg_csr* A, const double* x, const double* w, double* z,
                            double alpha, double beta, const tg_sched* s, void* workspace,
                            size_t workspace_bytes, tg_stream_t stream);
+/* The same with fp32 values, x, w, z and fp32 accumulation (the reference DSL's dtype
+ * "f32", tilegen/dsl.py:124-147; north_star: rel. error <= 1e-4). */
+TG_API int tg_fused_spmv_axpy_f32(const tg_csr* A, const float* x, const float* w, float* z, float alpha,
+                                  float beta, const tg_sched* s, void* workspace, size_t workspace_bytes,
+                                  tg_stream_t stream);
 /* C[i,:] = sum_p data[p] * B[indices[p],:]; B is cols x k, C is rows x k, row-major.
  * C is overwritten (ref: tilegen/codegen.py:646-685, math cpp/src/ref.cpp:31-43). */
 TG_API int tg_spmm_f32(const tg_csr* A, const float* B, float* C, int64_t k, const tg_sched* s,
@@ -154,13 +159,8 @@ TG_API int tg_sddmm_f64(const tg_csr* A, const double* U, const double* V, doubl
 /* z = alpha * x + beta * w (ref: tilegen/dsl.py:250-256, tilegen/codegen.py:580-589). */
 TG_API int tg_axpy_f64(const double* x, const double* w, double* z, double alpha, double beta,
                 int64_t n, const tg_sched* s, tg_stream_t stream);
-
-/* Measurement aid (no reference counterpart): *out += sum of x[indices[i]], i < n, with
- * the SpMV's gather path (same load instruction and L2 policy, four gathers in flight per
- * thread) and nothing else.  Timing it on a matrix's own column indices gives the
- * random-gather floor of that matrix's SpMV on this GPU; *out must be zeroed first. */
-TG_API int tg_gather_probe_f64(const int64_t* indices, int64_t n, const double* x, double* out,
-                               tg_stream_t stream);
+TG_API int tg_axpy_f32(const float* x, const float* w, float* z, float alpha, float beta, int64_t n,
+                       const tg_sched* s, tg_stream_t stream);
 
 /* ------------------------------------------------------ power iteration (new) */
 /* Iterated SpMV x <- A x / ||A x||, one process per GPU, rows split into `nparts`
@@ -197,8 +197,12 @@ TG_API int tg_power_finalize_f64(const double* x, int32_t nparts, int64_t stride
  * tile by tile and stores each tile into every y_peers[q], writes its slot to all
  * ranks, then stores `epoch` into flag_peers[q][rank] (system-scope release).  Call with
  * epoch = 1, 2, ... and alternate two iterate buffers.  A wait that runs out sets bit 4
- * (value 16) of the workspace's error word (read it with tg_power_error) and skips the
- * step.  Plain peer stores only: no multicast, no TMA. */
+ * (value 16) of the workspace's error word (read it with tg_power_error).  The error word
+ * is sticky: while it is set, every step and tg_p2p_wait on this workspace returns at once
+ * without computing, writing the slot or releasing a flag (so the peers give up in turn),
+ * and the kernel always leaves the workspace's ticket at zero.  To restart, every rank
+ * zeroes its flag array and calls tg_power_clear_error, then steps again from epoch 1.
+ * Plain peer stores only: no multicast, no TMA. */
 TG_API int tg_power_step_p2p_f64(const tg_csr* A, const double* x, int32_t nparts, int32_t rank,
                                  int64_t stride, double* const* y_peers, uint64_t* const* flag_peers,
                                  uint64_t epoch, const tg_sched* s, void* workspace,
@@ -206,8 +210,11 @@ TG_API int tg_power_step_p2p_f64(const tg_csr* A, const double* x, int32_t npart
 /* Copies the power workspace's error word to *err (synchronises `stream`): 16 = a peer
  * wait ran out.  Zero when nothing went wrong. */
 TG_API int tg_power_error(const void* workspace, uint32_t* err, tg_stream_t stream);
+/* Clears the power workspace's error word (asynchronously on `stream`). */
+TG_API int tg_power_clear_error(void* workspace, tg_stream_t stream);
 /* Bounded wait (2 s) until every entry of this rank's flag array reached `epoch`: the
- * pushes of the last step have landed and the local iterate is complete. */
+ * pushes of the last step have landed and the local iterate is complete.  Returns at once
+ * (error word unchanged) when the workspace's error word is already set. */
 TG_API int tg_p2p_wait(const uint64_t* flag_local, int32_t nparts, uint64_t epoch, void* workspace,
                        size_t workspace_bytes, tg_stream_t stream);
 
@@ -228,10 +235,12 @@ TG_API int tg_ipc_close(void* ptr);
  * until the process exits), so there is no workspace argument and nothing is allocated.
  * Limit: the partition of A's nonzeros must fit the array -- about 67 million nonzeros
  * with block_size 256, 33 million with 128; larger calls return TG_EINVAL naming the
- * limit.  The first call on a device looks up the array's address (cudaGetSymbolAddress)
- * and should come before any stream capture there.  All calls share the array, so calls
- * that overlap on the GPU race: order them on one stream.  Bounds checking and plan
- * reuse are not available here. */
+ * limit.  The schedule is resolved as for tg_spmv_f64 (NULL: the tg_set_schedule one),
+ * with the merge split forced.  The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress) and should come before any stream capture there; the address is
+ * cached for the process and does not survive cudaDeviceReset.  All calls share the array,
+ * so calls that overlap on the GPU race: order them on one stream.  Bounds checking and
+ * plan reuse are not available here. */
 TG_API int tg_spmv_f64_noalloc(const tg_csr* A, const double* x, double* y, const tg_sched* s,
                                tg_stream_t stream);
 

@@ -34,7 +34,10 @@ REF_DIR = os.path.join(ORACLE_DIR, "_ref")
 GEN_DIR = os.path.join(REF_DIR, "gen")
 ORACLE_LIB = os.path.join(BUILD_DIR, "liboracle.so")
 TGREF_LIB = os.path.join(REF_DIR, "libtgref.so")
-DEFAULT_REF_ROOT = os.environ.get("TILEGEN_REFERENCE_ROOT", "/root/reference")
+# The reference checkout: $TILEGEN_REFERENCE_ROOT, else a `reference` directory beside
+# this repository's root (the layout of a source checkout of both projects).
+DEFAULT_REF_ROOT = os.environ.get("TILEGEN_REFERENCE_ROOT",
+                                  os.path.join(os.path.dirname(os.path.dirname(ORACLE_DIR)), "reference"))
 
 # CPU schedules emitted for the reference OpenMP backend: the reference default
 # (tilegen/autotune.py:55-56) and two tiled/unrolled variants its CPU autotune explores

@@ -36,7 +36,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF_ROOT = os.environ.get("TILEGEN_REFERENCE_ROOT", "/root/reference")
+# the reference checkout: $TILEGEN_REFERENCE_ROOT, else `reference` beside this repository
+REF_ROOT = os.environ.get("TILEGEN_REFERENCE_ROOT", os.path.join(os.path.dirname(REPO), "reference"))
 
 
 def main() -> int:

@@ -1,5 +1,6 @@
-"""bench.py's workload definitions: compulsory bytes (SURVEY-style formulas restated from
-the BASELINE shapes), default schedules the library accepts, row sharding."""
+"""bench.py's workload definitions: compulsory bytes (indptr + indices + values + dense
+inputs + outputs, each once, at the BASELINE shapes), default schedules the library
+accepts, row sharding."""
 
 from __future__ import annotations
 

@@ -2,6 +2,9 @@
 
 from __future__ import annotations
 
+import ctypes
+import time
+
 import numpy as np
 import pytest
 import torch
@@ -150,6 +153,72 @@ def test_p2p_fused_step_emulated_on_one_gpu(parts):
     xr, nr = O.power_iteration(A, x0, iters)
     assert rel(x, xr) <= 1e-9
     assert abs(float(pis[0].result()[1]) - nr) <= 1e-9 * nr
+
+
+def _single_rank_p2p(A):
+    """One rank (nparts = 1) wired for the fused exchange with its own buffers and a
+    zeroed flag array."""
+    dev = torch.device("cuda")
+    pi = PowerIteration(torch.as_tensor(A.indptr).to(dev), torch.as_tensor(A.indices).to(dev),
+                        torch.as_tensor(A.data).to(dev), uniform_bounds(A.rows, 1), 0, sched=_sched(4, 2, 2),
+                        exchange=lambda x: None)
+    flags = [torch.zeros(1, dtype=torch.int64, device=dev)]
+    pi.p2p_setup([(pi.x[0], pi.x[1])], flags)
+    return pi, flags[0]
+
+
+def test_p2p_step_whose_wait_runs_out_reports_it_and_the_workspace_stays_usable():
+    """Failure detection of the fused exchange without a GPU fault: the step of epoch 3
+    waits for a flag >= 2 that nothing sets, so its bounded device wait (2 s) runs out.
+    Checks the error bit, that nothing was published, that later steps and waits return
+    at once while the error word is set, and that after a restart (flags zeroed, error
+    cleared) the same workspace gives the oracle's iterate (the ticket was not left
+    behind by the failed launch)."""
+    A = M.baseline_matrix("c3", scale=0.3)
+    pi, flag = _single_rank_p2p(A)
+    x0 = np.random.default_rng(9).uniform(-1, 1, A.rows)
+    dev = torch.device("cuda")
+    pi.set_x0(torch.as_tensor(x0).to(dev))
+    torch.cuda.synchronize()
+    pi.exchange_state.epoch = 2
+    t0 = time.perf_counter()
+    pi.p2p_step(0)  # epoch 3
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert pi.error_word() == 16
+    assert 1.5 <= waited < 20.0, waited
+    assert int(flag.item()) == 0  # no epoch published
+    t0 = time.perf_counter()
+    pi.p2p_step(1)  # epoch 4: the error word is set, so no wait
+    pi.p2p_wait()
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 1.0
+    assert pi.error_word() == 16 and int(flag.item()) == 0
+    # restart on the same workspace
+    pi.reset_exchange()
+    pi.set_x0(torch.as_tensor(x0).to(dev))
+    pi.iterate(6)
+    x, lam = pi.result()
+    assert pi.error_word() == 0 and int(flag.item()) == 6
+    xr, nr = O.power_iteration(A, x0, 6)
+    assert rel(x.cpu().numpy(), xr) <= 1e-9
+    assert abs(float(lam) - nr) <= 1e-9 * nr
+
+
+def test_p2p_wait_that_runs_out_sets_the_error_bit():
+    """tg_p2p_wait for an epoch no flag reaches gives up after its 2 s bound with bit 16
+    of the error word; the status of the (asynchronous) call itself is TG_OK."""
+    A = M.baseline_matrix("c3", scale=0.05)
+    pi, flag = _single_rank_p2p(A)
+    L = lib.load()
+    st = L.tg_p2p_wait(flag.data_ptr(), 1, 1, pi.ws.data_ptr(), pi.ws.numel(),
+                       torch.cuda.current_stream().cuda_stream)
+    assert st == lib.TG_OK
+    v = ctypes.c_uint32(0)
+    assert L.tg_power_error(pi.ws.data_ptr(), ctypes.byref(v), torch.cuda.current_stream().cuda_stream) == lib.TG_OK
+    assert v.value == 16
+    assert L.tg_power_clear_error(pi.ws.data_ptr(), torch.cuda.current_stream().cuda_stream) == lib.TG_OK
+    assert pi.error_word() == 0
 
 
 @pytest.mark.gpu

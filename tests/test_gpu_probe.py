@@ -1,10 +1,13 @@
-"""The gather-floor probe (tg_gather_probe_f64) gathers exactly the SpMV's x values."""
+"""The benchmark's gather-floor probe (libtg_gather_probe.so, tg_gather_probe_f64)
+gathers exactly the SpMV's x values; it lives outside the product library."""
 
 from __future__ import annotations
 
+import subprocess
+
 import pytest
 
-from tilegen_b200 import lib
+from tilegen_b200 import bench_probe, lib
 
 
 @pytest.mark.gpu
@@ -18,16 +21,20 @@ def test_gather_probe_sums_the_gathered_values(n):
     x = torch.rand(1 << 16, dtype=torch.float64, device=dev, generator=g)
     idx = torch.randint(0, x.numel(), (n,), device=dev, generator=g, dtype=torch.int64)
     out = torch.zeros(1, dtype=torch.float64, device=dev)
-    L = lib.load()
-    lib.check(L.tg_gather_probe_f64(idx.data_ptr(), n, x.data_ptr(), out.data_ptr(),
-                                    torch.cuda.current_stream().cuda_stream), "tg_gather_probe_f64")
+    bench_probe.gather_probe_f64(idx.data_ptr(), n, x.data_ptr(), out.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     ref = float(x[idx].sum()) if n else 0.0
     assert abs(float(out.item()) - ref) <= 1e-9 * max(1.0, abs(ref))
 
 
 def test_gather_probe_rejects_bad_arguments():
-    L = lib.load()
+    L = bench_probe.load()
     assert L.tg_gather_probe_f64(None, -1, None, None, None) == lib.TG_EINVAL
     assert L.tg_gather_probe_f64(None, 5, None, None, None) == lib.TG_EINVAL
     assert L.tg_gather_probe_f64(None, 0, None, None, None) == lib.TG_OK
+
+
+def test_probe_is_not_in_the_product_library():
+    out = subprocess.run(["nm", "-D", "--defined-only", lib.lib_path()], capture_output=True, text=True).stdout
+    assert "tg_gather_probe_f64" not in out

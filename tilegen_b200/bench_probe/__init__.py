@@ -1,0 +1,33 @@
+"""The benchmark's gather-floor probe (libtg_gather_probe.so): the random x gathers of a
+CSR SpMV and nothing else.  A measurement aid, kept out of libtilegen_b200.so."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+PROBE_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtg_gather_probe.so")
+
+_probe: Optional[ctypes.CDLL] = None
+
+
+def load() -> ctypes.CDLL:
+    """Load and type libtg_gather_probe.so (built by tilegen_b200.build)."""
+    global _probe
+    if _probe is None:
+        if not os.path.exists(PROBE_PATH):
+            raise OSError("libtg_gather_probe.so not found at %s; run `python -m tilegen_b200.build`" % PROBE_PATH)
+        L = ctypes.CDLL(PROBE_PATH)
+        fn = L.tg_gather_probe_f64
+        fn.restype = ctypes.c_int
+        fn.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        _probe = L
+    return _probe
+
+
+def gather_probe_f64(indices_ptr: int, n: int, x_ptr: int, out_ptr: int, stream: int) -> None:
+    """*out += sum of x[indices[i]] for i < n, on `stream` (device pointers)."""
+    rc = load().tg_gather_probe_f64(indices_ptr, n, x_ptr, out_ptr, stream)
+    if rc != 0:
+        raise RuntimeError("tg_gather_probe_f64 failed with status %d" % rc)

@@ -8,9 +8,17 @@
 // no row offsets, no row reductions, no output vector), so the time it takes is the
 // floor for the SpMV's gather traffic on this GPU.  Benchmarks report the SpMV's time
 // against it next to the HBM roofline.
+//
+// A measurement aid only: it is built into its own library (libtg_gather_probe.so, loaded
+// by the benchmark), not into libtilegen_b200.so.
+//
+//   int tg_gather_probe_f64(const int64_t* indices, int64_t n, const double* x, double* out,
+//                           void* stream);
+// *out += sum of x[indices[i]], i < n (device pointers; *out zeroed by the caller).
+// Returns 0, -1 for a bad argument, -2 when the launch failed.
 #include <algorithm>
 
-#include "tg_common.cuh"
+#include "../csrc/tg_common.cuh"
 
 namespace tg {
 namespace {
@@ -39,12 +47,12 @@ __global__ void __launch_bounds__(256) gather_probe_kernel(const int64_t* __rest
 
 using namespace tg;
 
-extern "C" int tg_gather_probe_f64(const int64_t* indices, int64_t n, const double* x, double* out,
-                                   tg_stream_t stream) {
-    if (n < 0) return set_error(TG_EINVAL, "tg_gather_probe_f64: negative n");
-    if (n > 0 && (!indices || !x || !out)) return set_error(TG_EINVAL, "tg_gather_probe_f64: null pointer argument");
+extern "C" __attribute__((visibility("default"))) int tg_gather_probe_f64(const int64_t* indices, int64_t n,
+                                                                         const double* x, double* out, void* stream) {
+    if (n < 0) return TG_EINVAL;
+    if (n > 0 && (!indices || !x || !out)) return TG_EINVAL;
     if (n == 0) return TG_OK;
     const int64_t blocks = std::min<int64_t>(ceil_div(n, 256 * 4), 148 * 16);
     gather_probe_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(indices, n, x, out);
-    return check_launch("gather_probe_kernel");
+    return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ECUDA;
 }

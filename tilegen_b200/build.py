@@ -90,7 +90,23 @@ def build(force: bool = False, jobs: int = 0, verbose: bool = False) -> str:
         if res.returncode != 0:
             raise RuntimeError("link failed:\n%s%s" % (res.stdout, res.stderr))
     build_cli(nvcc, force)
+    build_probe(nvcc, force)
     return LIB_PATH
+
+
+PROBE_SRC = os.path.join(PKG_DIR, "bench_probe", "tg_gather_probe.cu")
+PROBE_PATH = os.path.join(PKG_DIR, "bench_probe", "libtg_gather_probe.so")
+
+
+def build_probe(nvcc: str, force: bool = False) -> str:
+    """The benchmark's gather-floor probe, a library of its own (not part of
+    libtilegen_b200.so)."""
+    if force or _stale(PROBE_PATH, [PROBE_SRC, *_headers()]):
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, "-shared", "-cudart", "static", "-o", PROBE_PATH, PROBE_SRC]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError("gather probe build failed:\n%s%s" % (res.stdout, res.stderr))
+    return PROBE_PATH
 
 
 CLI_SRC = os.path.join(PKG_DIR, "cli", "tilegen_b200_bench.cpp")

@@ -17,7 +17,7 @@ Two ways in:
   reference's ``passes.run_pipeline`` -- the schedule transforms (Tile, ThreadsPerRow,
   Unroll, Vectorize, Parallelize) are read from ``kernel.schedule`` exactly as the
   reference's ``_lowering`` does (tilegen/codegen.py:119-134).  This is the entry a
-  maintainer calls from the reference's ``generate()``.
+  maintainer calls from the reference's ``generate()`` for ``backend == "b200"``.
 """
 
 from __future__ import annotations

@@ -49,8 +49,8 @@ template <typename T, bool AXPY>
 int spmv_run(const tg_csr& A, const T* x, T* y, const Epi<T, AXPY>& epi, const tg_sched& s, void* ws,
              size_t ws_bytes, cudaStream_t st);
 size_t spmv_ws_bytes(int64_t rows, int64_t nnz, const tg_sched& s, size_t elem);
-int axpy_run(const double* x, const double* w, double* z, double alpha, double beta, int64_t n, int block,
-             cudaStream_t st);
+template <typename T>
+int axpy_run(const T* x, const T* w, T* z, T alpha, T beta, int64_t n, int block, cudaStream_t st);
 // power iteration (tg_power.cu)
 size_t power_ws_bytes(int64_t nnz, const tg_sched& s);
 int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride, double* y, const tg_sched& s,
@@ -106,7 +106,12 @@ DeviceScratch* device_scratch() {
     return &g_dev[dev];
 }
 
-int resolve(const tg_sched* in, tg_sched* out) {
+}  // namespace
+
+// Fills *out from `in` (NULL: the process schedule of tg_set_schedule) with every zero
+// knob replaced by its default, and checks it.  Every tg_* entry point resolves its
+// schedule here.
+int resolve_schedule(const tg_sched* in, tg_sched* out) {
     tg_sched s;
     if (in) {
         s = *in;
@@ -141,6 +146,10 @@ int resolve(const tg_sched* in, tg_sched* out) {
     *out = s;
     return TG_OK;
 }
+
+namespace {
+
+int resolve(const tg_sched* in, tg_sched* out) { return resolve_schedule(in, out); }
 
 int check_csr(const tg_csr* A, const char* op) {
     if (!A) return set_error(TG_EINVAL, "%s: null CSR descriptor", op);
@@ -302,6 +311,14 @@ int tg_fused_spmv_axpy_f64(const tg_csr* A, const double* x, const double* w, do
     return spmv_run<double, true>(*A, x, z, Epi<double, true>{w, alpha, beta}, sc, workspace, workspace_bytes, st);
 }
 
+int tg_fused_spmv_axpy_f32(const tg_csr* A, const float* x, const float* w, float* z, float alpha, float beta,
+                           const tg_sched* s, void* workspace, size_t workspace_bytes, tg_stream_t stream) {
+    TG_PRELUDE("tg_fused_spmv_axpy_f32");
+    if (A->rows > 0 && (!z || !w)) return set_error(TG_EINVAL, "tg_fused_spmv_axpy_f32: null w/z");
+    if (A->nnz > 0 && !x) return set_error(TG_EINVAL, "tg_fused_spmv_axpy_f32: null x");
+    return spmv_run<float, true>(*A, x, z, Epi<float, true>{w, alpha, beta}, sc, workspace, workspace_bytes, st);
+}
+
 int tg_spmm_f32(const tg_csr* A, const float* B, float* C, int64_t k, const tg_sched* s, void* workspace,
                 size_t workspace_bytes, tg_stream_t stream) {
     TG_PRELUDE("tg_spmm_f32");
@@ -340,7 +357,18 @@ int tg_axpy_f64(const double* x, const double* w, double* z, double alpha, doubl
     if (n < 0) return set_error(TG_EINVAL, "tg_axpy_f64: negative n");
     if (n > 0 && (!x || !w || !z)) return set_error(TG_EINVAL, "tg_axpy_f64: null x/w/z");
     const int64_t n_eff = (sc.flags & TG_FLAG_INJECT_BUG) && n > 0 ? n - 1 : n;
-    return axpy_run(x, w, z, alpha, beta, n_eff, sc.block_size, static_cast<cudaStream_t>(stream));
+    return axpy_run<double>(x, w, z, alpha, beta, n_eff, sc.block_size, static_cast<cudaStream_t>(stream));
+}
+
+int tg_axpy_f32(const float* x, const float* w, float* z, float alpha, float beta, int64_t n, const tg_sched* s,
+                tg_stream_t stream) {
+    tg_sched sc;
+    int rc = resolve(s, &sc);
+    if (rc != TG_OK) return rc;
+    if (n < 0) return set_error(TG_EINVAL, "tg_axpy_f32: negative n");
+    if (n > 0 && (!x || !w || !z)) return set_error(TG_EINVAL, "tg_axpy_f32: null x/w/z");
+    const int64_t n_eff = (sc.flags & TG_FLAG_INJECT_BUG) && n > 0 ? n - 1 : n;
+    return axpy_run<float>(x, w, z, alpha, beta, n_eff, sc.block_size, static_cast<cudaStream_t>(stream));
 }
 
 size_t tg_power_workspace_bytes(int64_t nnz, const tg_sched* s) {
@@ -388,6 +416,12 @@ int tg_power_error(const void* workspace, uint32_t* err, tg_stream_t stream) {
     int rc = check_cuda(cudaMemcpyAsync(err, w, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync");
     if (rc != TG_OK) return rc;
     return check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+}
+
+int tg_power_clear_error(void* workspace, tg_stream_t stream) {
+    if (!workspace) return set_error(TG_EINVAL, "tg_power_clear_error: null workspace");
+    char* w = static_cast<char*>(workspace) + power_err_offset();
+    return check_cuda(cudaMemsetAsync(w, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream)), "cudaMemsetAsync");
 }
 
 int tg_p2p_wait(const uint64_t* flag_local, int32_t nparts, uint64_t epoch, void* workspace, size_t workspace_bytes,

@@ -13,7 +13,10 @@
 // * Host code cannot use the array's name as a device address.  The first call on a
 //   device looks the address up with cudaGetSymbolAddress while that device is current,
 //   checks the result and caches it; that first call should therefore come before any
-//   stream capture on the device.
+//   stream capture on the device.  The cached address belongs to the device's current
+//   context: after cudaDeviceReset (or anything else that destroys the primary context
+//   and reloads the module) it is stale, so such a program must not call this entry
+//   point again in the same process.
 // * Calls that need more scratch than the array holds are rejected with TG_EINVAL and a
 //   message giving the limit; nothing here calls cudaMalloc, cudaFree or any allocating
 //   routine.
@@ -31,6 +34,7 @@ int spmv_run(const tg_csr& A, const T* x, T* y, const Epi<T, AXPY>& epi, const t
              size_t ws_bytes, cudaStream_t st);
 int64_t merge_chunk_nnz(int block);
 int merge_block(const tg_sched& s);
+int resolve_schedule(const tg_sched* in, tg_sched* out);
 }  // namespace tg
 
 using namespace tg;
@@ -70,17 +74,13 @@ extern "C" int tg_spmv_f64_noalloc(const tg_csr* A, const double* x, double* y, 
         return set_error(TG_EINVAL, "tg_spmv_f64_noalloc: negative size");
     if (!A->indptr || (A->nnz > 0 && (!A->indices || !A->data || !x)) || (A->rows > 0 && !y))
         return set_error(TG_EINVAL, "tg_spmv_f64_noalloc: null pointer argument");
+    // the schedule tg_spmv_f64 would use (NULL: the process schedule), with the merge split
     tg_sched sc;
-    if (s) {
-        sc = *s;
-    } else {
-        tg_default_schedule(&sc);
-    }
+    int rc = resolve_schedule(s, &sc);
+    if (rc != TG_OK) return rc;
     sc.split = TG_SPLIT_MERGE;
     if (sc.flags & (TG_FLAG_BOUNDS_CHECK | TG_FLAG_REUSE_PLAN))
         return set_error(TG_EINVAL, "tg_spmv_f64_noalloc: bounds checking and plan reuse are not available here");
-    int rc = tg_validate_schedule(&sc);
-    if (rc != TG_OK) return rc;
     const int64_t S = merge_chunk_nnz(merge_block(sc));
     const int64_t nchunks = A->nnz > 0 ? ceil_div(A->nnz, S) : 0;
     const size_t need = A->nnz > 0 ? split_ws_bytes(nchunks, 1, sizeof(double)) : 0;

@@ -123,7 +123,14 @@ __global__ void __launch_bounds__(512) power_step_kernel(PowerArgs a) {
 //   3. each CTA fences (system scope) and takes a ticket; the last CTA sums the norm
 //      partials in CTA order, writes the slot to every rank, fences, and release-stores
 //      `epoch` into flag_peers[q][rank] for every q.
-// A wait that runs out sets bit 4 of *err and skips the step; the host reads *err.
+// Failure (a peer that stops answering).  A wait that runs out sets bit 4 of *err.  The
+// error word is sticky: a CTA that finds it set (at entry, or while it waits because
+// another CTA gave up) skips its rows without waiting any longer, so a failed launch
+// ends about 2 s after it started instead of 2 s per wave of CTAs.  Every CTA still
+// takes its ticket, so the ticket returns to zero at the end of every launch, and the
+// last CTA neither writes the slot nor publishes the epoch when *err is set: the peers
+// see no flag and give up in turn.  The host reads *err (tg_power_error) and clears it
+// (tg_power_clear_error) only after every rank agreed to restart from zeroed flags.
 struct PowerP2PArgs {
     const int64_t* indptr;
     const int64_t* indices;
@@ -152,6 +159,27 @@ __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned l
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+__device__ __forceinline__ uint32_t ld_err(const uint32_t* p) { return *reinterpret_cast<const volatile uint32_t*>(p); }
+
+// Bounded wait (2 s) until flag_local[q] >= need for every q < nparts.  Gives up at once
+// when *err is already set; sets bit 4 of *err when the time runs out.  Returns whether
+// the wait was met.
+__device__ __forceinline__ bool wait_flags(const unsigned long long* flag_local, int nparts, unsigned long long need,
+                                           uint32_t* err) {
+    if (ld_err(err) != 0u) return false;
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < nparts; ++q) {
+        while (ld_acquire_sys(&flag_local[q]) < need) {
+            if (ld_err(err) != 0u) return false;  // another CTA (or an earlier launch) gave up
+            if (globaltimer_ns() - t0 > 2000000000ull) {
+                atomicOr(err, 16u);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
 template <int TPR, int U, int V>
 __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
     constexpr int kGroups = 256 / TPR;  // rows per CTA tile: one per lane group
@@ -162,17 +190,7 @@ __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
     const uint64_t ps = policy_evict_first();
     const uint64_t pg = policy_evict_last();
     if (threadIdx.x == 0) {
-        int ok = 1;
-        const uint64_t t0 = globaltimer_ns();
-        for (int q = 0; q < a.nparts && ok; ++q) {
-            while (ld_acquire_sys(&a.flag_local[q]) + 1 < a.epoch) {
-                if (globaltimer_ns() - t0 > 2000000000ull) {
-                    ok = 0;
-                    atomicOr(a.err, 16u);
-                    break;
-                }
-            }
-        }
+        const int ok = wait_flags(a.flag_local, a.nparts, a.epoch - 1, a.err) ? 1 : 0;
         s_ok = ok;
         double t = 0.0;
         if (ok)
@@ -180,7 +198,6 @@ __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
         s_scale = t > 0.0 ? 1.0 / sqrt(t) : 0.0;
     }
     __syncthreads();
-    if (!s_ok) return;
     __threadfence_system();
     const double scale = s_scale;
     const int lane = threadIdx.x % TPR;
@@ -190,10 +207,11 @@ __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
     if constexpr (TPR < 32) mask = ((1u << TPR) - 1u) << ((threadIdx.x % 32) / TPR * TPR);
     const int64_t own = (int64_t)a.rank * a.stride;
     double sq = 0.0;
-    for (int64_t base = (int64_t)blockIdx.x * kGroups; base < a.rows; base += (int64_t)gridDim.x * kGroups) {
+    const int64_t rows = s_ok ? a.rows : 0;  // a CTA whose wait failed skips its rows
+    for (int64_t base = (int64_t)blockIdx.x * kGroups; base < rows; base += (int64_t)gridDim.x * kGroups) {
         const int64_t i = base + group;
         double v = 0.0;
-        if (i < a.rows) {
+        if (i < rows) {
             double acc = row_dot<double, TPR, U, V>(a.indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
             if constexpr (TPR > 1) acc = group_sum<TPR>(acc, mask);
             v = scale * acc;
@@ -205,7 +223,7 @@ __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
         const double mine = __shfl_sync(kFull, v, src);
         const int64_t row0 = base + (threadIdx.x / 32) * kWarpRows;
         const int64_t r = row0 + (wl % kWarpRows);
-        if (r < a.rows)
+        if (r < rows)
             for (int q = wl / kWarpRows; q < a.nparts; q += 32 / kWarpRows) a.y_peers[q][own + r] = mine;
     }
     const double part = block_sum(sq, s_warp);
@@ -218,30 +236,28 @@ __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
     __syncthreads();
     if (s_last && threadIdx.x < 32) {
         __threadfence_system();
-        double v = 0.0;
-        for (unsigned i = threadIdx.x; i < gridDim.x; i += 32) v += __ldcg(&a.partials[i]);
+        // every CTA set its error bit (if any) before its ticket: this read sees it
+        const bool failed = ld_err(a.err) != 0u;
+        if (!failed) {
+            double v = 0.0;
+            for (unsigned i = threadIdx.x; i < gridDim.x; i += 32) v += __ldcg(&a.partials[i]);
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off);  // every lane: the total
-        if (threadIdx.x < a.nparts) a.y_peers[threadIdx.x][own + a.stride - 1] = v;
-        __threadfence_system();
-        __syncwarp();
-        if (threadIdx.x < a.nparts) st_release_sys(&a.flag_peers[threadIdx.x][a.rank], a.epoch);
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off);  // every lane: the total
+            if (threadIdx.x < a.nparts) a.y_peers[threadIdx.x][own + a.stride - 1] = v;
+            __threadfence_system();
+            __syncwarp();
+            if (threadIdx.x < a.nparts) st_release_sys(&a.flag_peers[threadIdx.x][a.rank], a.epoch);
+        }
         if (threadIdx.x == 0) *a.ticket = 0u;
     }
 }
 
 // Bounded wait (2 s) until every rank's flag reached `epoch` (the last iteration's
-// pushes have all landed); bit 4 of *err on timeout.
+// pushes have all landed); bit 4 of *err on timeout, and no wait at all when *err is
+// already set.
 __global__ void p2p_wait_kernel(const unsigned long long* flag_local, int nparts, unsigned long long epoch,
                                 uint32_t* err) {
-    const uint64_t t0 = globaltimer_ns();
-    for (int q = 0; q < nparts; ++q)
-        while (ld_acquire_sys(&flag_local[q]) < epoch)
-            if (globaltimer_ns() - t0 > 2000000000ull) {
-                atomicOr(err, 16u);
-                return;
-            }
-    __threadfence_system();
+    if (wait_flags(flag_local, nparts, epoch, err)) __threadfence_system();
 }
 
 // slot <- sum(shard[0..rows)^2), same deterministic reduction.

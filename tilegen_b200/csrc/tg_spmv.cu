@@ -219,8 +219,9 @@ __global__ void fill_rows_kernel(T* y, int64_t rows, int64_t row_limit, Epi<T, A
         y[r] = epi(T(0), r);
 }
 
-__global__ void axpy_kernel(const double* __restrict__ x, const double* __restrict__ w, double* __restrict__ z,
-                            double alpha, double beta, int64_t n) {
+template <typename T>
+__global__ void axpy_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ z, T alpha, T beta,
+                            int64_t n) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         z[i] = alpha * x[i] + beta * w[i];
 }
@@ -383,13 +384,17 @@ template int spmv_run<double, true>(const tg_csr&, const double*, double*, const
                                     const tg_sched&, void*, size_t, cudaStream_t);
 template int spmv_run<float, false>(const tg_csr&, const float*, float*, const Epi<float, false>&, const tg_sched&,
                                     void*, size_t, cudaStream_t);
+template int spmv_run<float, true>(const tg_csr&, const float*, float*, const Epi<float, true>&, const tg_sched&,
+                                   void*, size_t, cudaStream_t);
 
-int axpy_run(const double* x, const double* w, double* z, double alpha, double beta, int64_t n, int block,
-             cudaStream_t st) {
+template <typename T>
+int axpy_run(const T* x, const T* w, T* z, T alpha, T beta, int64_t n, int block, cudaStream_t st) {
     if (n == 0) return TG_OK;
     int64_t blocks = std::min<int64_t>(ceil_div(n, block), 148 * 16);
-    axpy_kernel<<<(unsigned)blocks, block, 0, st>>>(x, w, z, alpha, beta, n);
+    axpy_kernel<T><<<(unsigned)blocks, block, 0, st>>>(x, w, z, alpha, beta, n);
     return check_launch("axpy_kernel");
 }
+template int axpy_run<double>(const double*, const double*, double*, double, double, int64_t, int, cudaStream_t);
+template int axpy_run<float>(const float*, const float*, float*, float, float, int64_t, int, cudaStream_t);
 
 }  // namespace tg

@@ -444,5 +444,7 @@ template int stream_run<double, kPower>(const tg_csr&, const double*, double*, c
                                         int64_t, const tg_sched&, void*, size_t, cudaStream_t);
 template int stream_run<float, kPlain>(const tg_csr&, const float*, float*, const float*, float, float, int,
                                        int64_t, const tg_sched&, void*, size_t, cudaStream_t);
+template int stream_run<float, kAxpy>(const tg_csr&, const float*, float*, const float*, float, float, int,
+                                       int64_t, const tg_sched&, void*, size_t, cudaStream_t);
 
 }  // namespace tg

@@ -145,21 +145,23 @@ def spmv(A: DeviceCSR, x: torch.Tensor, y: Optional[torch.Tensor] = None, sched=
 def fused_spmv_axpy(A: DeviceCSR, x: torch.Tensor, w: torch.Tensor, alpha: float, beta: float,
                     z: Optional[torch.Tensor] = None, sched=None, stream=None,
                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """z = alpha * (A x) + beta * w (fp64)."""
+    """z = alpha * (A x) + beta * w (fp64, or fp32 with fp32 accumulation when A.data is
+    float32)."""
     L = _lib.load()
     dev = A.device
+    dt = A.data.dtype
     s = _sched(sched)
-    _check_vec(x, A.cols, torch.float64, dev, "x")
-    _check_vec(w, A.rows, torch.float64, dev, "w")
+    _check_vec(x, A.cols, dt, dev, "x")
+    _check_vec(w, A.rows, dt, dev, "w")
     if z is None:
-        z = torch.empty(A.rows, dtype=torch.float64, device=dev)
-    _check_vec(z, A.rows, torch.float64, dev, "z")
+        z = torch.empty(A.rows, dtype=dt, device=dev)
+    _check_vec(z, A.rows, dt, dev, "z")
     nbytes = L.tg_spmv_workspace_bytes(A.rows, A.nnz, ctypes.byref(s))
     wp, wn = _ws(nbytes, dev, workspace)
     desc = A.desc()
-    _lib.check(L.tg_fused_spmv_axpy_f64(ctypes.byref(desc), x.data_ptr(), w.data_ptr(), z.data_ptr(), float(alpha),
-                                        float(beta), ctypes.byref(s), wp, wn, _stream_ptr(stream, dev)),
-               "tg_fused_spmv_axpy_f64")
+    fn = L.tg_fused_spmv_axpy_f64 if dt == torch.float64 else L.tg_fused_spmv_axpy_f32
+    _lib.check(fn(ctypes.byref(desc), x.data_ptr(), w.data_ptr(), z.data_ptr(), float(alpha), float(beta),
+                  ctypes.byref(s), wp, wn, _stream_ptr(stream, dev)), "tg_fused_spmv_axpy")
     return z
 
 
@@ -212,16 +214,20 @@ def sddmm(A: DeviceCSR, U: torch.Tensor, V: torch.Tensor, out: Optional[torch.Te
 
 def axpy(x: torch.Tensor, w: torch.Tensor, alpha: float, beta: float, z: Optional[torch.Tensor] = None,
          sched=None, stream=None) -> torch.Tensor:
-    """z = alpha x + beta w (fp64)."""
+    """z = alpha x + beta w (fp64, or fp32 when x is float32)."""
     L = _lib.load()
     dev = x.device
+    dt = x.dtype
+    if dt not in (torch.float64, torch.float32):
+        raise ValueError("axpy operands must be float64 or float32 (got %s)" % dt)
     s = _sched(sched)
     n = x.numel()
-    _check_vec(x, n, torch.float64, dev, "x")
-    _check_vec(w, n, torch.float64, dev, "w")
+    _check_vec(x, n, dt, dev, "x")
+    _check_vec(w, n, dt, dev, "w")
     if z is None:
-        z = torch.empty(n, dtype=torch.float64, device=dev)
-    _check_vec(z, n, torch.float64, dev, "z")
-    _lib.check(L.tg_axpy_f64(x.data_ptr(), w.data_ptr(), z.data_ptr(), float(alpha), float(beta), n,
-                             ctypes.byref(s), _stream_ptr(stream, dev)), "tg_axpy_f64")
+        z = torch.empty(n, dtype=dt, device=dev)
+    _check_vec(z, n, dt, dev, "z")
+    fn = L.tg_axpy_f64 if dt == torch.float64 else L.tg_axpy_f32
+    _lib.check(fn(x.data_ptr(), w.data_ptr(), z.data_ptr(), float(alpha), float(beta), n, ctypes.byref(s),
+                  _stream_ptr(stream, dev)), "tg_axpy")
     return z

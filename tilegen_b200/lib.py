@@ -106,8 +106,6 @@ SIGNATURES = {
                                          ctypes.c_void_p, _SP, ctypes.c_double]),
     "tg_renumber_columns": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                            ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p]),
-    "tg_gather_probe_f64": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
-                                           ctypes.c_void_p]),
     "tg_default_schedule": (None, [_SP]),
     "tg_validate_schedule": (ctypes.c_int, [_SP]),
     "tg_set_schedule": (ctypes.c_int, [_SP]),
@@ -118,11 +116,13 @@ SIGNATURES = {
     "tg_spmv_f64": (ctypes.c_int, [_CP, _P, _P, _SP, _P, _SZ, _P]),
     "tg_spmv_f32": (ctypes.c_int, [_CP, _P, _P, _SP, _P, _SZ, _P]),
     "tg_fused_spmv_axpy_f64": (ctypes.c_int, [_CP, _P, _P, _P, _F64, _F64, _SP, _P, _SZ, _P]),
+    "tg_fused_spmv_axpy_f32": (ctypes.c_int, [_CP, _P, _P, _P, ctypes.c_float, ctypes.c_float, _SP, _P, _SZ, _P]),
     "tg_spmm_f32": (ctypes.c_int, [_CP, _P, _P, _I64, _SP, _P, _SZ, _P]),
     "tg_spmm_f64": (ctypes.c_int, [_CP, _P, _P, _I64, _SP, _P, _SZ, _P]),
     "tg_sddmm_f32": (ctypes.c_int, [_CP, _P, _P, _P, _I64, _SP, _P, _SZ, _P]),
     "tg_sddmm_f64": (ctypes.c_int, [_CP, _P, _P, _P, _I64, _SP, _P, _SZ, _P]),
     "tg_axpy_f64": (ctypes.c_int, [_P, _P, _P, _F64, _F64, _I64, _SP, _P]),
+    "tg_axpy_f32": (ctypes.c_int, [_P, _P, _P, ctypes.c_float, ctypes.c_float, _I64, _SP, _P]),
     "tg_power_workspace_bytes": (_SZ, [_I64, _SP]),
     "tg_power_step_f64": (ctypes.c_int, [_CP, _P, ctypes.c_int32, _I64, _P, _SP, _P, _SZ, _P]),
     "tg_shard_norm2_f64": (ctypes.c_int, [_P, _I64, _I64, _P, _SZ, _P]),
@@ -131,6 +131,7 @@ SIGNATURES = {
                                              ctypes.c_uint64, _SP, _P, _SZ, _P]),
     "tg_p2p_wait": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_uint64, _P, _SZ, _P]),
     "tg_power_error": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
+    "tg_power_clear_error": (ctypes.c_int, [_P, _P]),
     "tg_peer_buffer_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(ctypes.c_void_p)]),
     "tg_peer_buffer_free": (ctypes.c_int, [_P]),
     "tg_ipc_get_handle": (ctypes.c_int, [_P, ctypes.c_char_p]),

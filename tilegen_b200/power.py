@@ -325,10 +325,26 @@ class PowerIteration:
         return self._ex
 
     def error_word(self) -> int:
+        """The workspace's error word (synchronises the stream): 16 = a bounded wait for
+        the peers ran out.  While it is set, fused steps and waits return at once."""
         L = self._lib.load()
         v = ctypes.c_uint32(0)
         self._lib.check(L.tg_power_error(self.ws.data_ptr(), ctypes.byref(v), self._stream()), "tg_power_error")
         return int(v.value)
+
+    def clear_error(self) -> None:
+        """Clear the error word.  A restart after a failed exchange also needs every
+        rank's flag array zeroed and the epoch counter reset (reset_exchange)."""
+        L = self._lib.load()
+        self._lib.check(L.tg_power_clear_error(self.ws.data_ptr(), self._stream()), "tg_power_clear_error")
+
+    def reset_exchange(self) -> None:
+        """Zero this rank's flag array, restart the epoch count at 0 and clear the error
+        word: the local half of a restart, which every rank must do (with its kernels
+        finished) before any rank steps again."""
+        self._ex.flags_local.zero_()
+        self._ex.epoch = 0
+        self.clear_error()
 
     # -- iteration ---------------------------------------------------------------------
     def set_x0(self, x0_local) -> None:
