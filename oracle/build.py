@@ -51,7 +51,7 @@ REF_CPU_CONFIGS: Dict[str, Dict[str, int]] = {
     "T128U4": dict(tile_size=128, threads_per_row=1, unroll=4, vector_width=1, block_size=512),
 }
 REF_KERNELS_F64 = ["spmv", "spmm", "sddmm", "fused_spmv_axpy", "axpy"]
-REF_KERNELS_F32 = ["spmv", "spmm", "sddmm"]
+REF_KERNELS_F32 = ["spmv", "spmm", "sddmm", "fused_spmv_axpy", "axpy"]
 
 
 def _run(cmd: List[str]) -> None:
@@ -100,6 +100,23 @@ def _ref_kernel(ref_dsl, name: str, dtype: str):
         V = d.dense_tensor("V", shape=(N, K), dtype=dtype)
         C = d.sparse_tensor("C", d.CSR, shape=(M, N), dtype=dtype)
         return d.kernel("sddmm", [d.assign(C[i, j], A[i, j] * d.reduce_sum(k, U[i, k] * V[j, k]))])
+    if name == "fused_spmv_axpy":  # tilegen/dsl.py:237-247
+        A = d.sparse_tensor("A", d.CSR, shape=(M, N), dtype=dtype)
+        x = d.dense_tensor("x", shape=(N,), dtype=dtype)
+        w = d.dense_tensor("w", shape=(M,), dtype=dtype)
+        z = d.dense_tensor("z", shape=(M,), dtype=dtype)
+        alpha = d.scalar_tensor("alpha", dtype=dtype)
+        beta = d.scalar_tensor("beta", dtype=dtype)
+        t = d.dense_tensor("t", shape=(M,), dtype=dtype)
+        return d.kernel("fused_spmv_axpy", [d.assign(t[i], d.reduce_sum(j, A[i, j] * x[j])),
+                                            d.assign(z[i], alpha * t[i] + beta * w[i])])
+    if name == "axpy":  # tilegen/dsl.py:250-256
+        x = d.dense_tensor("x", shape=(M,), dtype=dtype)
+        w = d.dense_tensor("w", shape=(M,), dtype=dtype)
+        z = d.dense_tensor("z", shape=(M,), dtype=dtype)
+        alpha = d.scalar_tensor("alpha", dtype=dtype)
+        beta = d.scalar_tensor("beta", dtype=dtype)
+        return d.kernel("axpy", [d.assign(z[i], alpha * x[i] + beta * w[i])])
     raise ValueError(name)
 
 

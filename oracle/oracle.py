@@ -180,14 +180,16 @@ class RefOmpKernel:
     """A reference OpenMP ``launch_<kernel>`` called on host buffers, with the argument
     order of tilegen/verify.py:166-173 (``float*`` instead of ``double*`` for f32)."""
 
-    def __init__(self, path: str, kernel: str):
+    def __init__(self, path: str, kernel: str, dtype: str = "f64"):
         self.path = path
         self.kernel = kernel
         self.lib = ctypes.CDLL(path)
         self.fn = getattr(self.lib, "launch_%s" % kernel)
+        # the scalars alpha/beta have the kernel's dtype (tilegen/codegen.py:270-271)
+        S = F64 if dtype == "f64" else ctypes.c_float
         nptr = {"spmv": 5, "spmm": 5, "sddmm": 6, "fused_spmv_axpy": 6, "axpy": 3}[kernel]
         tail = {"spmv": [I64] * 3, "spmm": [I64] * 4, "sddmm": [I64] * 4,
-                "fused_spmv_axpy": [F64, F64, I64, I64, I64], "axpy": [F64, F64, I64]}[kernel]
+                "fused_spmv_axpy": [S, S, I64, I64, I64], "axpy": [S, S, I64]}[kernel]
         self.fn.argtypes = [P] * nptr + tail
         self.fn.restype = None
 

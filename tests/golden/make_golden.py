@@ -139,10 +139,13 @@ def main() -> int:
         Cc = np.zeros((M_, K), npdt); k(ip, ix, dd, BB, Cc, M_, N_, K, ix.size); omp["spmm_" + dtype] = Cc
         k = O.RefOmpKernel(libs["ref_omp_sddmm_%s_T32U1" % dtype], "sddmm")
         o = np.zeros(ix.size, npdt); k(ip, ix, dd, UU, VV, o, M_, N_, K, ix.size); omp["sddmm_" + dtype] = o
-    k = O.RefOmpKernel(libs["ref_omp_fused_spmv_axpy_f64_T32U1"], "fused_spmv_axpy")
-    z = np.zeros(M_); k(ip, ix, dv, x, w, z, alpha, beta, M_, N_, ix.size); omp["fused_spmv_axpy_f64"] = z
-    k = O.RefOmpKernel(libs["ref_omp_axpy_f64_T32U1"], "axpy")
-    z = np.zeros(M_); k(x, w, z, alpha, beta, M_); omp["axpy_f64"] = z
+    for dtype, npdt in (("f64", np.float64), ("f32", np.float32)):
+        dd, xx, ww = dv.astype(npdt), x.astype(npdt), w.astype(npdt)
+        k = O.RefOmpKernel(libs["ref_omp_fused_spmv_axpy_%s_T32U1" % dtype], "fused_spmv_axpy", dtype)
+        z = np.zeros(M_, npdt); k(ip, ix, dd, xx, ww, z, alpha, beta, M_, N_, ix.size)
+        omp["fused_spmv_axpy_" + dtype] = z
+        k = O.RefOmpKernel(libs["ref_omp_axpy_%s_T32U1" % dtype], "axpy", dtype)
+        z = np.zeros(M_, npdt); k(xx, ww, z, alpha, beta, M_); omp["axpy_" + dtype] = z
     np.savez_compressed(
         os.path.join(HERE, "edge257.npz"),
         indptr=ip, indices=ix, data=dv, shape=np.array(A.shape, np.int64), K=np.int64(K),

@@ -86,9 +86,10 @@ def test_kernel_matches_float64_reference(kernel, cfg, edge, edge_csr):
     check_f64(out, edge["ref_" + kernel], edge_csr)
 
 
-@pytest.mark.parametrize("kernel", ["spmv", "spmm", "sddmm"])
-@pytest.mark.parametrize("cfg", [REF_SCHEDULES[0], REF_SCHEDULES[3], B200_SCHEDULES[0], B200_SCHEDULES[1]],
-                         ids=["T32", "T128-TPR8", "merge256", "merge128"])
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("cfg", [REF_SCHEDULES[0], REF_SCHEDULES[3], B200_SCHEDULES[0], B200_SCHEDULES[1],
+                                 B200_SCHEDULES[5]],
+                         ids=["T32", "T128-TPR8", "merge256", "merge128", "stream"])
 def test_fp32_accumulation_within_1e_4(kernel, cfg, edge, edge_csr):
     c = cg.Config(**{**cfg.to_dict(), "dtype": "f32"})
     out = run_kernel(cg.generate(kernel, c), edge_csr, edge_data(edge), K=8)
