@@ -66,9 +66,9 @@ typedef void* tg_stream_t;
 /* flags */
 #define TG_FLAG_BOUNDS_CHECK 1u /* validate indptr/indices on the device; TG_EBOUNDS on error */
 #define TG_FLAG_INJECT_BUG 2u   /* deliberately skip the last row (harness self-test) */
-#define TG_FLAG_REUSE_PLAN 4u   /* stream split: the workspace already holds this matrix's
-                                   partition from an earlier call with the same A and
-                                   schedule; skip the analysis pass */
+#define TG_FLAG_REUSE_PLAN 4u   /* SpMV merge and stream splits: the workspace already holds
+                                   this matrix's partition from an earlier call with the
+                                   same A and schedule; skip the analysis pass */
 
 /*
  * Mirrors tilegen.codegen.Lowering (tilegen/codegen.py:90-134): each knob of the

@@ -221,13 +221,16 @@ def test_merge_results_are_deterministic():
     assert np.array_equal(run_kernel(g, m, data), run_kernel(g, m, data))
 
 
-def test_stream_plan_reuse_flag():
+@pytest.mark.parametrize("cfg", [cg.Config(split="stream", unroll=4), cg.Config(split="merge", block_size=128),
+                                 cg.Config(split="merge", block_size=256)], ids=["stream", "merge128", "merge256"])
+def test_plan_reuse_flag(cfg):
     """TG_FLAG_REUSE_PLAN skips the analysis pass on a workspace planned for the same
-    matrix; results are identical to a planned call."""
+    matrix; results are identical to a planned call (the merge split's arrival counters
+    are back at zero after every call)."""
     m = _long_row_matrix()
     A = D.DeviceCSR.from_host(m, "cuda")
     x = torch.as_tensor(np.random.default_rng(3).uniform(-1, 1, m.cols)).cuda()
-    s = cg.generate("spmv", cg.Config(split="stream", unroll=4)).sched
+    s = cg.generate("spmv", cfg).sched
     L = lib.load()
     nb = L.tg_spmv_workspace_bytes(m.rows, m.nnz, ctypes.byref(s))
     ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
@@ -244,6 +247,37 @@ def test_stream_plan_reuse_flag():
 def test_dense_widths(K, split):
     m = M.baseline_matrix("c3", scale=0.02)
     data = inputs_for("spmm", m, K, 5)
+    for dtype in ("f64", "f32"):
+        cfg = cg.Config(threads_per_row=32, unroll=2, vector_width=4, split=split, dtype=dtype)
+        for kernel, ref in (("spmm", O.spmm(m, data[2])), ("sddmm", O.sddmm(m, data[3], data[4]))):
+            out = run_kernel(cg.generate(kernel, cfg), m, data, K=K)
+            if dtype == "f64":
+                check_f64(out, ref, m)
+            else:
+                assert rel_err(out, ref) <= 1e-4, (kernel, K, split)
+
+
+def _wide_matrix():
+    """2000 rows over 1,000,000 columns (power-law row lengths, a few long rows): the
+    dense operand of SpMM/SDDMM has 1M rows, so K of 24 or more fp32 columns (12 or more
+    fp64) exceeds the 64 MB L2 budget and the call runs over column tiles."""
+    rng = np.random.default_rng(31)
+    rows, cols = 2000, 1_000_000
+    lens = np.minimum(np.floor(1.0 / rng.uniform(size=rows)).astype(np.int64), 3000)
+    lens[7] = 2600
+    indptr = np.zeros(rows + 1, np.int64)
+    np.cumsum(lens, out=indptr[1:])
+    idx = np.concatenate([np.sort(rng.choice(cols, size=L, replace=False)) for L in lens]).astype(np.int64)
+    return M.CSR(indptr, idx, rng.uniform(-1, 1, idx.size), (rows, cols), "wide")
+
+
+@pytest.mark.parametrize("K", [8, 24, 40, 64, 100])
+@pytest.mark.parametrize("split", ["rowwise", "merge"])
+def test_column_tiling(K, split):
+    """SpMM and SDDMM over column tiles (one launch per tile; SDDMM accumulates each
+    nonzero's dot product across the tiles) against the oracle, fp64 and fp32."""
+    m = _wide_matrix()
+    data = inputs_for("spmm", m, K, 6)
     for dtype in ("f64", "f32"):
         cfg = cg.Config(threads_per_row=32, unroll=2, vector_width=4, split=split, dtype=dtype)
         for kernel, ref in (("spmm", O.spmm(m, data[2])), ("sddmm", O.sddmm(m, data[3], data[4]))):

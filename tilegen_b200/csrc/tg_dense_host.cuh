@@ -20,8 +20,30 @@ struct DenseChoice {
     int G, VEC, NCV, U, block;
     bool merge;
     int64_t S;
-    int64_t ktile;  // columns per launch (SpMM column tiling)
+    int64_t ktile;  // columns per launch (column tiling)
 };
+
+// Bytes of the gathered dense operand (B for SpMM, V for SDDMM) one launch may touch:
+// above it the call runs over column tiles whose slab (cols x tile columns) fits, so the
+// slab stays in the 126 MB L2 while the CSR stream flows past it with evict_first.
+#ifndef TG_DENSE_L2_BUDGET
+#define TG_DENSE_L2_BUDGET (64ll << 20)
+#endif
+
+// Columns per launch: K when cols x K elements fit the budget, else the widest tile of
+// 64-byte multiples (two L2 sectors per gathered row slice) that fits, balanced so the
+// tiles have equal width.
+inline int64_t dense_ktile(int64_t K, int64_t cols, size_t elem) {
+    const int64_t budget = TG_DENSE_L2_BUDGET;
+    const int64_t gran = 64 / (int64_t)elem;  // elements per 64 bytes
+    if (budget <= 0 || cols <= 0 || K <= gran || cols * K * (int64_t)elem <= budget) return K;
+    int64_t kmax = budget / (cols * (int64_t)elem);
+    kmax = std::max<int64_t>(gran, kmax / gran * gran);
+    const int64_t ntiles = (K + kmax - 1) / kmax;
+    int64_t kt = (K + ntiles - 1) / ntiles;
+    kt = (kt + gran - 1) / gran * gran;
+    return std::min(kt, K);
+}
 
 inline int pow2_floor(int v) {
     int p = 1;
@@ -49,22 +71,30 @@ inline int64_t default_dense_chunk(int64_t nnz, bool is_spmm) {
     return S;
 }
 
+// `cols` is the row count of the gathered operand (A's columns); 0 = no column tiling
+// (workspace sizing, which must bound every tiling).
 template <typename T>
-DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void* p0, const void* p1, int64_t nnz) {
+DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void* p0, const void* p1, int64_t nnz,
+                         int64_t cols = 0) {
     DenseChoice d{};
     const int vmax = sizeof(T) == 4 ? 4 : 2;
+    const int64_t kt = dense_ktile(K, cols, sizeof(T));
     int vec = std::min(std::max(s.vector_width, 1), vmax);
     vec = pow2_floor(vec);
-    while (vec > 1 && (K % vec != 0 || !aligned_to(p0, vec * sizeof(T)) || !aligned_to(p1, vec * sizeof(T))))
+    // every tile starts at a multiple of kt, so vectors must divide kt as well as K
+    while (vec > 1 && (K % vec != 0 || kt % vec != 0 || !aligned_to(p0, vec * sizeof(T)) ||
+                       !aligned_to(p1, vec * sizeof(T))))
         vec /= 2;
     d.VEC = vec;
-    const int64_t nvec = (K + vec - 1) / vec;  // column vectors per row
+    const int64_t nvec = (kt + vec - 1) / vec;  // column vectors per row of one tile
     int g = pow2_floor(std::min(std::max(s.threads_per_row, 4), 32));
     g = std::max(4, std::min(g, pow2_ceil(nvec)));
     d.G = g;
     const int64_t per_lane = (nvec + g - 1) / g;
     d.NCV = per_lane <= 1 ? 1 : (per_lane <= 2 ? 2 : 4);
-    d.ktile = is_spmm ? std::min<int64_t>(K, (int64_t)g * vec * d.NCV) : K;
+    // SpMM covers at most G*VEC*NCV columns per launch (its accumulators live in
+    // registers); SDDMM loops over its tile inside the kernel
+    d.ktile = is_spmm ? std::min<int64_t>(kt, (int64_t)g * vec * d.NCV) : kt;
     d.U = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
     d.block = (s.block_size >= 512) ? 512 : (s.block_size >= 256 ? 256 : 128);
     d.merge = (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM);
@@ -147,13 +177,36 @@ size_t dense_ws_bytes(int64_t rows, int64_t nnz, int64_t K, const tg_sched& s, b
     return split_ws_bytes(nchunks, width, sizeof(T));
 }
 
+// One launch per column tile [k0, k0 + ktile).  SpMM writes C's columns of the tile;
+// SDDMM accumulates each nonzero's dot product over the tiles in order (kPass*).
+template <typename T>
+int launch_tiles(const DenseChoice& d, bool is_spmm, const DenseArgs<T>& a, const T* B, const T* U, T* C, int64_t K,
+                 cudaStream_t st) {
+    const int64_t ntiles = (K + d.ktile - 1) / d.ktile;
+    for (int64_t ti = 0; ti < ntiles; ++ti) {
+        const int64_t k0 = ti * d.ktile;
+        DenseArgs<T> t = a;
+        t.B = B + k0;
+        t.U = is_spmm ? U : U + k0;
+        t.C = is_spmm ? C + k0 : C;
+        t.kt = std::min(d.ktile, K - k0);
+        t.pass = ntiles == 1 ? kPassOnly : (ti == 0 ? kPassFirst : (ti == ntiles - 1 ? kPassLast : kPassMid));
+        if (!dense_dispatch<T>(d, is_spmm, t, st))
+            return set_error(TG_EUNSUPPORTED, "no %s instance for G=%d VEC=%d NCV=%d U=%d", is_spmm ? "spmm" : "sddmm",
+                             d.G, d.VEC, d.NCV, d.U);
+        int rc = check_launch(is_spmm ? "spmm_kernel" : "sddmm_kernel");
+        if (rc != TG_OK) return rc;
+    }
+    return TG_OK;
+}
+
 // C = A * B (SpMM) or out = A .* (U V^T) on A's pattern (SDDMM, B = V).
 template <typename T>
 int dense_run(bool is_spmm, const tg_csr& A, const T* B, const T* U, T* C, int64_t K, const tg_sched& s, void* ws,
               size_t ws_bytes, cudaStream_t st) {
     if (K <= 0) return set_error(TG_EINVAL, "dense width K must be positive (got %lld)", (long long)K);
     if (A.rows == 0) return TG_OK;
-    const DenseChoice d = choose_dense<T>(s, K, is_spmm, B, is_spmm ? (const void*)C : (const void*)U, A.nnz);
+    const DenseChoice d = choose_dense<T>(s, K, is_spmm, B, is_spmm ? (const void*)C : (const void*)U, A.nnz, A.cols);
     DenseArgs<T> a{};
     a.indptr = A.indptr;
     a.indices = A.indices;
@@ -188,33 +241,9 @@ int dense_run(bool is_spmm, const tg_csr& A, const T* B, const T* U, T* C, int64
         if (is_spmm && A.nnz == 0) {
             // every row is empty: C = 0 through the rowwise kernel (it writes empty rows)
         }
-        for (int64_t k0 = 0; k0 < (is_spmm ? K : 1); k0 += d.ktile) {
-            DenseArgs<T> t = a;
-            t.B = B + (is_spmm ? k0 : 0);
-            t.U = U;
-            t.C = C + (is_spmm ? k0 : 0);
-            t.kt = is_spmm ? std::min(d.ktile, K - k0) : K;
-            if (!dense_dispatch<T>(dr, is_spmm, t, st))
-                return set_error(TG_EUNSUPPORTED, "no %s instance for G=%d VEC=%d NCV=%d U=%d",
-                                 is_spmm ? "spmm" : "sddmm", d.G, d.VEC, d.NCV, d.U);
-            int rc = check_launch(is_spmm ? "spmm_kernel" : "sddmm_kernel");
-            if (rc != TG_OK) return rc;
-        }
-        return TG_OK;
+        return launch_tiles<T>(dr, is_spmm, a, B, U, C, K, st);
     }
-    for (int64_t k0 = 0; k0 < (is_spmm ? K : 1); k0 += d.ktile) {
-        DenseArgs<T> t = a;
-        t.B = B + (is_spmm ? k0 : 0);
-        t.U = U;
-        t.C = C + (is_spmm ? k0 : 0);
-        t.kt = is_spmm ? std::min(d.ktile, K - k0) : K;
-        if (!dense_dispatch<T>(d, is_spmm, t, st))
-            return set_error(TG_EUNSUPPORTED, "no %s instance for G=%d VEC=%d NCV=%d U=%d", is_spmm ? "spmm" : "sddmm",
-                             d.G, d.VEC, d.NCV, d.U);
-        int rc = check_launch(is_spmm ? "spmm_kernel" : "sddmm_kernel");
-        if (rc != TG_OK) return rc;
-    }
-    return TG_OK;
+    return launch_tiles<T>(d, is_spmm, a, B, U, C, K, st);
 }
 
 }  // namespace tg

@@ -16,6 +16,11 @@
 // SpMM writes C (no pre-zeroing needed); rows split across chunks are reduced with the
 // deterministic last-arriver protocol using K-wide partial rows.  SDDMM writes one value
 // per nonzero in A's order, so the output pattern is A's by construction.
+//
+// Column tiling (host side, tg_dense_host.cuh): when the gathered operand (B or V) is
+// larger than an L2 budget, the call is split into launches over column tiles whose
+// slab of it fits in L2, so each dense row is fetched from DRAM about once instead of
+// once per nonzero that touches it; the CSR stream is re-read per tile.
 #pragma once
 
 #include "tg_split.cuh"
@@ -38,11 +43,18 @@ struct DenseArgs {
     int64_t S;       // merge: nonzeros per chunk
     int64_t nunits;  // rows (rowwise) or chunks (merge)
     int64_t row_limit;
+    int pass;        // SDDMM column tile: kPassOnly / kPassFirst / kPassMid / kPassLast
     const int64_t* own_first;
     int* cnt;
     T* head;
     T* tail;
 };
+
+// SDDMM over column tiles.  Each nonzero's dot product is accumulated in out[p] across
+// the launches, one tile after the other (a fixed order), and A's value is applied by
+// the last one: only tile: out = a * dot; first: out = dot; middle: out += dot; last:
+// out = a * (out + dot).
+constexpr int kPassOnly = 0, kPassFirst = 1, kPassMid = 2, kPassLast = 3;
 
 template <int G>
 __device__ __forceinline__ unsigned group_mask() {
@@ -254,7 +266,7 @@ __global__ void __launch_bounds__(512) sddmm_kernel(DenseArgs<T> a) {
                 crow[u] = r;
                 if (q < ce) {
                     cidx[u] = ld_stream(a.indices + q, ps);
-                    cval[u] = ld_stream(a.data + q, ps);
+                    if (a.pass == kPassOnly || a.pass == kPassLast) cval[u] = ld_stream(a.data + q, ps);
                     if constexpr (MERGE) {
                         while (nxt <= q) {
                             ++r;
@@ -284,7 +296,17 @@ __global__ void __launch_bounds__(512) sddmm_kernel(DenseArgs<T> a) {
             for (int u = 0; u < U; ++u) {
                 T d = group_sum<G>(dot[u].get(), gmask);
                 const int64_t q = q0 + u;
-                if (lane == (u % G) && q < ce && crow[u] < a.row_limit) a.C[q] = cval[u] * d;
+                if (lane == (u % G) && q < ce && crow[u] < a.row_limit) {
+                    if (a.pass == kPassOnly) {
+                        a.C[q] = cval[u] * d;
+                    } else if (a.pass == kPassFirst) {
+                        a.C[q] = d;
+                    } else if (a.pass == kPassMid) {
+                        a.C[q] += d;
+                    } else {
+                        a.C[q] = cval[u] * (a.C[q] + d);
+                    }
+                }
             }
         }
     }

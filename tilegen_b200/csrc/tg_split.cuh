@@ -12,11 +12,10 @@
 // A row whose nonzeros cross chunk boundaries (a SPLIT row spanning chunks ca..cb) gets
 // one partial sum per chunk: tail[ca] from its owner, head[c] from each later chunk, and
 // the row is tail[ca] + head[ca+1] + ... + head[cb] in that fixed order (deterministic).
-// SpMV publishes the partials and sums them in a fix-up kernel launched right behind the
-// merge kernel (cnt[c] then holds the index of chunk c's split row).  SpMM/SDDMM, whose
-// CTAs are long-lived, sum them in place: every contributor publishes its partial,
-// fences and arrives on cnt[ca], and the last of the (cb - ca + 1) arrivals adds them
-// and writes the row; it also resets cnt[ca] to zero.
+// The partials are summed in place: every contributor publishes its partial and arrives
+// on one counter of the row (SpMV: cnt[cb], with an acq_rel atomic; SpMM/SDDMM: cnt[ca],
+// after a fence), and the last of the (cb - ca + 1) arrivals adds them, writes the row
+// and resets the counter to zero, so the counters are zero after every call.
 #pragma once
 
 #include "tg_common.cuh"

@@ -13,11 +13,11 @@
 //  * merge    -- nnz-balanced chunks of S = B*I nonzeros per CTA.  The CTA computes
 //    the chunk's products into shared memory (I coalesced loads and I gathers in flight
 //    per thread), then sums each row's piece from shared memory: short pieces by one
-//    thread, long ones by a warp.  A row crossing chunk boundaries gets
-//    one partial per chunk, which a small fix-up kernel launched right behind (with
-//    programmatic serialisation, so its launch overlaps the merge kernel) adds in chunk
-//    order.  Power-law rows of any length cost the same per nonzero as short rows, and
-//    no CTA waits on a fence or an atomic.
+//    thread, long ones by a warp.  A row crossing chunk boundaries gets one partial per
+//    chunk; the last of its contributors to arrive (acq_rel atomic) adds them in chunk
+//    order and writes the row, inside the same kernel.  Power-law rows of any length cost
+//    the same per nonzero as short rows, and no CTA ever waits for another.  The
+//    partition table (the plan) can be kept across calls on the same matrix.
 #include <algorithm>
 
 #include "tg_rowdot.cuh"
@@ -74,17 +74,52 @@ constexpr int kMergeI = 7;  // nonzeros per thread
 // pieces by a whole warp.
 constexpr int kShortPiece = 16;
 
+// Arrival count at which every contributor of a split row has published its partial:
+// the owner adds kArriveAll - (number of later chunks the row covers), each later chunk
+// adds 1, so the sum reaches kArriveAll exactly once, at the last arrival.
+constexpr int kArriveAll = 1 << 30;
+
+__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// A row whose nonzeros cross chunk boundaries spans chunks ca..cb: its owner ca publishes
+// tail[ca], every later chunk c' publishes head[c'], and each then arrives on cnt[cb]
+// (one split row ends in a chunk, so cb names the row).  The arrival is an acq_rel
+// atomic: it releases this contributor's partial and, for the last arrival, acquires
+// every other one.  The last arrival adds tail[ca] + head[ca+1] + ... + head[cb] in that
+// fixed order (the result does not depend on which contributor came last), writes the
+// row and resets cnt[cb] for the next call.
+template <typename T, bool AXPY>
+__device__ __forceinline__ void merge_arrive(const SpmvArgs<T>& a, const Epi<T, AXPY>& epi, int64_t r, int64_t ca,
+                                             int64_t cb, int64_t c, int64_t S, T v) {
+    (c == ca ? a.tail : a.head)[c] = v;
+    const int add = (c == ca) ? kArriveAll - (int)(cb - ca) : 1;
+    const int old = atomic_add_acq_rel(&a.cnt[cb], add);
+    if (old + add != kArriveAll) return;
+    if (ca < 0) ca = a.indptr[r] / S;  // a head contributor came last: find the owner
+    Sum<T> sum;
+    sum.add(ld_cg(&a.tail[ca]));
+    add_partials(sum, a.head + ca + 1, cb - ca, 1);
+    if (r < a.row_limit) a.y[r] = epi(sum.get(), r);
+    a.cnt[cb] = 0;
+}
+
 // Chunk c holds nonzeros [c*S, c*S + S) with S = B*I.  Its CTA
-//  1. computes the S products data[q] * x[indices[q]] into shared memory (each thread
-//     keeps I coalesced loads and then I gathers in flight);
-//  2. reads the offsets of the rows that start in the chunk (partition table);
-//  3. sums every row piece from shared memory in index order: short pieces by one
+//  1. issues the chunk's coalesced index/value loads (I per thread) and, at the same
+//     time, the loads of its rows' offsets (partition table, then the indptr slice of
+//     the rows that start in the chunk), then the I gathers of x, and stores the S
+//     products in shared memory;
+//  2. sums every row piece from shared memory in index order: short pieces by one
 //     thread, long pieces by a warp (strided partial sums, then a fixed shuffle tree).
-// A row that lies inside the chunk is written to y.  The piece of a row that started
-// in an earlier chunk (the chunk's head) and the piece of the chunk's last row when it
-// continues into later chunks (its tail) are published as partials for the fix-up
-// kernel.  Step 1 does not need the partition table, so it overlaps the partition
-// kernel (programmatic launch); the CTA never waits on another CTA.
+// A row that lies inside the chunk is written to y.  The piece of a row that started in
+// an earlier chunk (the chunk's head) and the piece of the chunk's last row when it
+// continues into later chunks (its tail) are combined with the row's other pieces by
+// merge_arrive, in this kernel: no fix-up launch.  On a planning call the partition
+// kernel runs just before (programmatic launch) and the table is read after pdl_wait;
+// with the plan reused there is no kernel before it and pdl_wait returns at once.
 template <typename T, bool AXPY, int B>
 __global__ void __launch_bounds__(B) spmv_merge_kernel(SpmvArgs<T> a, Epi<T, AXPY> epi) {
     constexpr int I = kMergeI;
@@ -103,43 +138,37 @@ __global__ void __launch_bounds__(B) spmv_merge_kernel(SpmvArgs<T> a, Epi<T, AXP
     const int n_items = (int)(ce - cs);
     const uint64_t ps = policy_evict_first();
     const uint64_t pg = policy_evict_last();
-    pdl_trigger();  // the fix-up kernel behind this one may be scheduled now
 
-    // 1. products
-    {
-        int64_t col[I];
-        T val[I];
+    // 1. CSR stream loads, then the row offsets (independent of them), then the gathers
+    int64_t col[I];
+    T val[I];
 #pragma unroll
-        for (int k = 0; k < I; ++k) {
-            const int q = tid + k * B;
-            col[k] = 0;
-            val[k] = T(0);
-            if (q < n_items) {
-                col[k] = ld_stream(a.indices + cs + q, ps);
-                val[k] = ld_stream(a.data + cs + q, ps);
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < I; ++k) {
-            const int q = tid + k * B;
-            if (q < n_items) s_prod[q] = val[k] * ld_gather(a.x + col[k], pg);
+    for (int k = 0; k < I; ++k) {
+        const int q = tid + k * B;
+        col[k] = 0;
+        val[k] = T(0);
+        if (q < n_items) {
+            col[k] = ld_stream(a.indices + cs + q, ps);
+            val[k] = ld_stream(a.data + cs + q, ps);
         }
     }
-    if (tid == 0) s_nlong = 0;
-
-    // 2. offsets of the rows starting in the chunk: indptr[of0 .. of1].  The partition
-    //    table is written by the kernel launched just before this one, so wait for it.
-    pdl_wait();
+    pdl_wait();  // planning call: the partition kernel before this one wrote the table
     const int64_t of0 = a.own_first[c];
     const int64_t of1 = a.own_first[c + 1];
     const int64_t n_off = of1 - of0 + 1;
     const bool off_smem = n_off <= RCAP;
     if (off_smem)
         for (int64_t j = tid; j < n_off; j += B) s_off[j] = a.indptr[of0 + j];
+    if (tid == 0) s_nlong = 0;
+#pragma unroll
+    for (int k = 0; k < I; ++k) {
+        const int q = tid + k * B;
+        if (q < n_items) s_prod[q] = val[k] * ld_gather(a.x + col[k], pg);
+    }
     __syncthreads();
     const int64_t* off = off_smem ? s_off : (a.indptr + of0);
 
-    // 3. pieces: task 0 is the head (rows before of0 continuing into the chunk), task
+    // 2. pieces: task 0 is the head (the row before of0, continuing into the chunk), task
     //    1 + j is row of0 + j.  Piece [lo, hi) in chunk coordinates.
     const int64_t ntask = n_off;  // head + (of1 - of0) rows
     auto piece = [&](int64_t t, int& lo, int& hi) {
@@ -152,15 +181,14 @@ __global__ void __launch_bounds__(B) spmv_merge_kernel(SpmvArgs<T> a, Epi<T, AXP
         }
     };
     auto finish = [&](int64_t t, T v) {
-        if (t == 0) {
-            a.head[c] = v;
+        if (t == 0) {  // head: row of0 - 1 ends in chunk (off[0] - 1) / S, owner unknown here
+            merge_arrive<T, AXPY>(a, epi, of0 - 1, -1, (off[0] - 1) / S, c, S, v);
         } else {
             const int64_t r = of0 + t - 1;
             if (off[t] <= ce) {
                 if (r < a.row_limit) a.y[r] = epi(v, r);
-            } else {
-                a.tail[c] = v;  // the chunk's last row continues past the chunk
-                a.cnt[c] = (int)t;
+            } else {  // the chunk's last row continues past the chunk
+                merge_arrive<T, AXPY>(a, epi, r, c, (off[t] - 1) / S, c, S, v);
             }
         }
     };
@@ -187,27 +215,6 @@ __global__ void __launch_bounds__(B) spmv_merge_kernel(SpmvArgs<T> a, Epi<T, AXP
         for (int q = lo + lane; q < hi; q += kWarp) sum.add(s_prod[q]);
         const T v = group_sum<kWarp>(sum.get(), kFull);
         if (lane == 0) finish(t, v);
-    }
-}
-
-// Rows split across chunks: chunk c's tail partial plus the head partials of the chunks
-// c+1..cb that the row covers, added in that order (the sums the merge kernel published),
-// one thread per chunk.  Launched right behind the merge kernel with programmatic
-// serialisation; everything before pdl_wait overlaps the merge kernel.
-template <typename T, bool AXPY>
-__global__ void __launch_bounds__(256) spmv_fixup_kernel(SpmvArgs<T> a, Epi<T, AXPY> epi, int64_t nchunks,
-                                                          int64_t S) {
-    pdl_wait();
-    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks;
-         c += (int64_t)gridDim.x * blockDim.x) {
-        const int code = a.cnt[c];  // 1 + the split row's index among the chunk's own rows
-        if (code == 0) continue;
-        const int64_t r = a.own_first[c] + code - 1;
-        const int64_t cb = (a.indptr[r + 1] - 1) / S;
-        Sum<T> sum;
-        sum.add(a.tail[c]);
-        add_partials(sum, a.head + c + 1, cb - c, 1);
-        if (r < a.row_limit) a.y[r] = epi(sum.get(), r);
     }
 }
 
@@ -333,16 +340,23 @@ int spmv_run(const tg_csr& A, const T* x, T* y, const Epi<T, AXPY>& epi, const t
         const size_t need = split_ws_bytes(nchunks, 1, sizeof(T));
         if (ws == nullptr || ws_bytes < need)
             return set_error(TG_ENOMEM, "spmv merge split needs %zu workspace bytes, got %zu", need, ws_bytes);
+        if (nchunks > 0x7fffffff) return set_error(TG_EINVAL, "too many chunks (%lld)", (long long)nchunks);
         SplitWs w = split_ws_carve(ws, nchunks, 1, sizeof(T));
-        int rc = launch_partition(A.indptr, A.rows, A.nnz, S, w, st);
-        if (rc != TG_OK) return rc;
+        // The plan (partition table, zeroed arrival counters) depends only on A's row
+        // offsets and the chunk size.  TG_FLAG_REUSE_PLAN: the workspace already holds it
+        // from an earlier call on the same A with the same schedule; every call leaves
+        // the counters at zero again.
+        const bool reuse = (s.flags & TG_FLAG_REUSE_PLAN) != 0;
+        if (!reuse) {
+            int rc = launch_partition(A.indptr, A.rows, A.nnz, S, w, st);
+            if (rc != TG_OK) return rc;
+        }
         a.own_first = w.own_first;
         a.cnt = w.cnt;
         a.head = static_cast<T*>(w.head);
         a.tail = static_cast<T*>(w.tail);
         a.err = w.err;
-        if (nchunks > 0x7fffffff) return set_error(TG_EINVAL, "too many chunks (%lld)", (long long)nchunks);
-        // programmatic launch: the chunk staging of the merge kernel overlaps the partition
+        // planning call: programmatic launch, so the chunk loads overlap the partition
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -351,18 +365,12 @@ int spmv_run(const tg_csr& A, const T* x, T* y, const Epi<T, AXPY>& epi, const t
         cfg.blockDim = dim3((unsigned)B);
         cfg.dynamicSmemBytes = 0;
         cfg.stream = st;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.attrs = reuse ? nullptr : attr;
+        cfg.numAttrs = reuse ? 0 : 1;
         cudaError_t e = B == 128 ? cudaLaunchKernelEx(&cfg, spmv_merge_kernel<T, AXPY, 128>, a, epi)
                                  : cudaLaunchKernelEx(&cfg, spmv_merge_kernel<T, AXPY, 256>, a, epi);
         if (e != cudaSuccess) return check_cuda(e, "spmv_merge_kernel launch");
-        rc = check_launch("spmv_merge_kernel");
-        if (rc != TG_OK) return rc;
-        cfg.gridDim = dim3((unsigned)std::min<int64_t>(ceil_div(nchunks, 256), 148 * 8));
-        cfg.blockDim = dim3(256);
-        e = cudaLaunchKernelEx(&cfg, spmv_fixup_kernel<T, AXPY>, a, epi, nchunks, S);
-        if (e != cudaSuccess) return check_cuda(e, "spmv_fixup_kernel launch");
-        return check_launch("spmv_fixup_kernel");
+        return check_launch("spmv_merge_kernel");
     }
     // rowwise
     const int tpr = s.threads_per_row;
