@@ -62,13 +62,17 @@ typedef void* tg_stream_t;
 #define TG_SPLIT_MERGE 1   /* nnz-balanced chunks, rows split across chunks + fix-up */
 #define TG_SPLIT_AUTO 2    /* library picks: the merge split (any row-length distribution) */
 #define TG_SPLIT_STREAM 3  /* SpMV: persistent TMA-fed row-block kernel; merge for SpMM/SDDMM */
+#define TG_SPLIT_BLOCK 4   /* SpMM: groups of 8 consecutive rows with one shared column list
+                              (block-structured matrices) gather each dense row once for the
+                              whole group; other groups row by row.  Merge for SpMV/SDDMM. */
 
 /* flags */
 #define TG_FLAG_BOUNDS_CHECK 1u /* validate indptr/indices on the device; TG_EBOUNDS on error */
 #define TG_FLAG_INJECT_BUG 2u   /* deliberately skip the last row (harness self-test) */
-#define TG_FLAG_REUSE_PLAN 4u   /* SpMV merge and stream splits: the workspace already holds
-                                   this matrix's partition from an earlier call with the
-                                   same A and schedule; skip the analysis pass */
+#define TG_FLAG_REUSE_PLAN 4u   /* SpMV merge / stream and SpMM block splits: the workspace
+                                   already holds this matrix's plan (partition or row-group
+                                   flags) from an earlier call with the same A and schedule;
+                                   skip the analysis pass */
 
 /*
  * Mirrors tilegen.codegen.Lowering (tilegen/codegen.py:90-134): each knob of the

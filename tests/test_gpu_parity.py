@@ -258,9 +258,8 @@ def test_dense_widths(K, split):
 
 
 def _wide_matrix():
-    """2000 rows over 1,000,000 columns (power-law row lengths, a few long rows): the
-    dense operand of SpMM/SDDMM has 1M rows, so K of 24 or more fp32 columns (12 or more
-    fp64) exceeds the 64 MB L2 budget and the call runs over column tiles."""
+    """2000 rows over 1,000,000 columns (power-law row lengths, a few long rows): a dense
+    operand of 1M rows, larger than L2 for every K here."""
     rng = np.random.default_rng(31)
     rows, cols = 2000, 1_000_000
     lens = np.minimum(np.floor(1.0 / rng.uniform(size=rows)).astype(np.int64), 3000)
@@ -273,9 +272,9 @@ def _wide_matrix():
 
 @pytest.mark.parametrize("K", [8, 24, 40, 64, 100])
 @pytest.mark.parametrize("split", ["rowwise", "merge"])
-def test_column_tiling(K, split):
-    """SpMM and SDDMM over column tiles (one launch per tile; SDDMM accumulates each
-    nonzero's dot product across the tiles) against the oracle, fp64 and fp32."""
+def test_wide_dense_operand(K, split):
+    """SpMM and SDDMM gathering from a 1M-row dense operand (SpMM with K above one lane
+    group's width runs one launch per column slab) against the oracle, fp64 and fp32."""
     m = _wide_matrix()
     data = inputs_for("spmm", m, K, 6)
     for dtype in ("f64", "f32"):
@@ -286,6 +285,70 @@ def test_column_tiling(K, split):
                 check_f64(out, ref, m)
             else:
                 assert rel_err(out, ref) <= 1e-4, (kernel, K, split)
+
+
+def _mixed_group_matrix():
+    """Row groups of 8 that share a column list (8x8 blocks) next to groups that do not
+    (one row of a group differs in one column, or in its length), a partial last group
+    and empty rows."""
+    rng = np.random.default_rng(41)
+    rows = []
+    for g in range(40):
+        cols = np.sort(rng.choice(5000, size=int(rng.integers(0, 40)), replace=False))
+        grp = [cols.copy() for _ in range(8)]
+        if g % 3 == 1 and cols.size:
+            grp[5] = np.sort(np.unique(np.append(cols[:-1], (cols[-1] + 1) % 5000)))
+        elif g % 3 == 2:
+            grp[2] = np.sort(rng.choice(5000, size=int(rng.integers(1, 60)), replace=False))
+        rows.extend(grp)
+    rows.extend([np.sort(rng.choice(5000, size=7, replace=False)) for _ in range(5)])
+    indptr = np.zeros(len(rows) + 1, np.int64)
+    np.cumsum([r.size for r in rows], out=indptr[1:])
+    idx = np.concatenate(rows).astype(np.int64)
+    return M.CSR(indptr, idx, rng.uniform(-1, 1, idx.size), (len(rows), 5000), "mixed_groups")
+
+
+@pytest.mark.parametrize("K", [8, 100, 128, 300])
+@pytest.mark.parametrize("name", ["blocked", "mixed", "edge", "c3"])
+def test_block_split_spmm(K, name, edge_csr):
+    """SpMM over row groups (TG_SPLIT_BLOCK): groups of 8 rows with one column list share
+    each gathered B row; the rest go row by row.  Against the oracle in fp64 and fp32;
+    the plan (group flags) reused on a second call gives identical output."""
+    m = {"blocked": lambda: M.make_matrix("blocked"), "mixed": _mixed_group_matrix, "edge": lambda: edge_csr,
+         "c3": lambda: M.baseline_matrix("c3", scale=0.02)}[name]()
+    data = inputs_for("spmm", m, K, 9)
+    ref = O.spmm(m, data[2])
+    for dtype in ("f64", "f32"):
+        cfg = cg.Config(split="block", dtype=dtype)
+        out = run_kernel(cg.generate("spmm", cfg), m, data, K=K)
+        if dtype == "f64":
+            check_f64(out, ref, m)
+        else:
+            assert rel_err(out, ref) <= 1e-4, (name, K)
+    # plan reuse
+    dev = torch.device("cuda")
+    A = D.DeviceCSR.from_host(m, dev)
+    Bd = torch.as_tensor(data[2]).to(dev)
+    s = cg.generate("spmm", cg.Config(split="block")).sched
+    L = lib.load()
+    ws = torch.zeros(max(1, int(L.tg_spmm_workspace_bytes(m.rows, m.nnz, K, ctypes.byref(s)))), dtype=torch.uint8,
+                     device=dev)
+    C1 = D.spmm(A, Bd, sched=s, workspace=ws)
+    s.flags |= lib.TG_FLAG_REUSE_PLAN
+    C2 = D.spmm(A, Bd, sched=s, workspace=ws)
+    assert torch.equal(C1, C2)
+
+
+def test_block_split_matches_rowwise_bitwise():
+    """Each row is summed over its nonzeros in index order on both paths, so the block
+    split's output equals the rowwise kernel's bit for bit."""
+    m = M.make_matrix("blocked")
+    data = inputs_for("spmm", m, 128, 2)
+    for dtype in ("f64", "f32"):
+        a = run_kernel(cg.generate("spmm", cg.Config(split="block", dtype=dtype)), m, data, K=128)
+        b = run_kernel(cg.generate("spmm", cg.Config(threads_per_row=32, vector_width=4, dtype=dtype)), m, data,
+                       K=128)
+        assert np.array_equal(a, b), dtype
 
 
 def test_misaligned_operands_use_safe_paths():

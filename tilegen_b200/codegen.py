@@ -32,6 +32,7 @@ from . import lib as _lib
 
 __all__ = [
     "Config",
+    "as_config",
     "Lowering",
     "B200Kernel",
     "STANDARD_KERNELS",
@@ -63,7 +64,7 @@ STANDARD_KERNELS: Dict[str, str] = {
 # vectorize pass keeps Vectorize for, tilegen/passes.py:348-396).
 _HAS_2D_DENSE = {"spmm", "sddmm"}
 _SPLITS = {"rowwise": _lib.TG_SPLIT_ROWWISE, "merge": _lib.TG_SPLIT_MERGE, "auto": _lib.TG_SPLIT_AUTO,
-           "stream": _lib.TG_SPLIT_STREAM}
+           "stream": _lib.TG_SPLIT_STREAM, "block": _lib.TG_SPLIT_BLOCK}
 
 
 @dataclass
@@ -72,7 +73,8 @@ class Config:
 
     ``split`` chooses the row mapping of the b200 kernels ("rowwise": the reference's
     T/TPR mapping; "merge": nnz-balanced chunks; "stream": the persistent TMA-fed SpMV,
-    merge for SpMM/SDDMM; "auto": merge), ``chunk_nnz`` the merge chunk size for
+    merge for SpMM/SDDMM; "block": SpMM over groups of 8 rows sharing a column list
+    (block-structured matrices), merge for SpMV/SDDMM; "auto": merge), ``chunk_nnz`` the merge chunk size for
     SpMM/SDDMM, ``bounds_check`` a device-side CSR validation before the call."""
 
     tile_size: int = 32
@@ -263,9 +265,25 @@ def generate(kernel, config: Config, backend: str = "b200", outdir: Optional[str
     return gen
 
 
-def generate_from_lowered(optimized_kernel, config: Config) -> B200Kernel:
+def as_config(config) -> Config:
+    """This package's Config from any object with the reference Config's fields
+    (tilegen/codegen.py:61-69: tile_size, threads_per_row, unroll, vector_width,
+    block_size, dtype, inject_bug); the b200-only knobs take their defaults unless the
+    object has them."""
+    if isinstance(config, Config):
+        return config
+    d = Config()
+    kw = {f: getattr(config, f, getattr(d, f)) for f in
+          ("tile_size", "threads_per_row", "unroll", "vector_width", "block_size", "dtype", "inject_bug", "split",
+           "chunk_nnz", "bounds_check")}
+    return Config(**kw)
+
+
+def generate_from_lowered(optimized_kernel, config) -> B200Kernel:
     """Build the descriptor from a kernel the reference's pass pipeline already lowered
-    (reads ``optimized_kernel.schedule`` and ``.pass_log``)."""
+    (reads ``optimized_kernel.schedule`` and ``.pass_log``).  ``config`` may be the
+    reference's own Config object."""
+    config = as_config(config)
     name = optimized_kernel.name
     if name not in STANDARD_KERNELS:
         raise NotImplementedError("the b200 backend has kernels for %s (got %r)" % (sorted(STANDARD_KERNELS), name))

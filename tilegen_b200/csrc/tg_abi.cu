@@ -140,8 +140,10 @@ int resolve_schedule(const tg_sched* in, tg_sched* out) {
         return set_error(TG_EINVAL, "block_size must be a multiple of 32 in [32, 512] (got %d)", s.block_size);
     if (s.block_size % tpr != 0)
         return set_error(TG_EINVAL, "block_size (%d) not divisible by threads_per_row (%d)", s.block_size, tpr);
-    if (s.split != TG_SPLIT_ROWWISE && s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_STREAM)
-        return set_error(TG_EINVAL, "split must be TG_SPLIT_ROWWISE, _MERGE, _STREAM or _AUTO (got %d)", s.split);
+    if (s.split != TG_SPLIT_ROWWISE && s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_STREAM &&
+        s.split != TG_SPLIT_BLOCK)
+        return set_error(TG_EINVAL, "split must be TG_SPLIT_ROWWISE, _MERGE, _STREAM, _BLOCK or _AUTO (got %d)",
+                         s.split);
     if (s.chunk_nnz < 0) return set_error(TG_EINVAL, "chunk_nnz must be >= 0 (got %d)", s.chunk_nnz);
     *out = s;
     return TG_OK;

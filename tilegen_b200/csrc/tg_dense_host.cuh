@@ -7,7 +7,9 @@
 //          operand alignment; 2 at most for fp64),
 //   U   -> nonzeros whose gathers are in flight per group (1, 2 or 4),
 //   B   -> threads per CTA (128, 256 or 512),
-//   split / chunk_nnz -> rowwise (one group per row) or merge (one group per chunk).
+//   split / chunk_nnz -> rowwise (one group per row) or merge (one group per chunk);
+//          block (SpMM): a warp per group of kGroupRows rows sharing each gathered row;
+//          SDDMM takes block as merge.
 #pragma once
 
 #include <algorithm>
@@ -20,30 +22,8 @@ struct DenseChoice {
     int G, VEC, NCV, U, block;
     bool merge;
     int64_t S;
-    int64_t ktile;  // columns per launch (column tiling)
+    int64_t ktile;  // SpMM columns per launch (what a lane group's accumulators cover)
 };
-
-// Bytes of the gathered dense operand (B for SpMM, V for SDDMM) one launch may touch:
-// above it the call runs over column tiles whose slab (cols x tile columns) fits, so the
-// slab stays in the 126 MB L2 while the CSR stream flows past it with evict_first.
-#ifndef TG_DENSE_L2_BUDGET
-#define TG_DENSE_L2_BUDGET (64ll << 20)
-#endif
-
-// Columns per launch: K when cols x K elements fit the budget, else the widest tile of
-// 64-byte multiples (two L2 sectors per gathered row slice) that fits, balanced so the
-// tiles have equal width.
-inline int64_t dense_ktile(int64_t K, int64_t cols, size_t elem) {
-    const int64_t budget = TG_DENSE_L2_BUDGET;
-    const int64_t gran = 64 / (int64_t)elem;  // elements per 64 bytes
-    if (budget <= 0 || cols <= 0 || K <= gran || cols * K * (int64_t)elem <= budget) return K;
-    int64_t kmax = budget / (cols * (int64_t)elem);
-    kmax = std::max<int64_t>(gran, kmax / gran * gran);
-    const int64_t ntiles = (K + kmax - 1) / kmax;
-    int64_t kt = (K + ntiles - 1) / ntiles;
-    kt = (kt + gran - 1) / gran * gran;
-    return std::min(kt, K);
-}
 
 inline int pow2_floor(int v) {
     int p = 1;
@@ -71,33 +51,27 @@ inline int64_t default_dense_chunk(int64_t nnz, bool is_spmm) {
     return S;
 }
 
-// `cols` is the row count of the gathered operand (A's columns); 0 = no column tiling
-// (workspace sizing, which must bound every tiling).
 template <typename T>
-DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void* p0, const void* p1, int64_t nnz,
-                         int64_t cols = 0) {
+DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void* p0, const void* p1, int64_t nnz) {
     DenseChoice d{};
     const int vmax = sizeof(T) == 4 ? 4 : 2;
-    const int64_t kt = dense_ktile(K, cols, sizeof(T));
     int vec = std::min(std::max(s.vector_width, 1), vmax);
     vec = pow2_floor(vec);
-    // every tile starts at a multiple of kt, so vectors must divide kt as well as K
-    while (vec > 1 && (K % vec != 0 || kt % vec != 0 || !aligned_to(p0, vec * sizeof(T)) ||
-                       !aligned_to(p1, vec * sizeof(T))))
+    while (vec > 1 && (K % vec != 0 || !aligned_to(p0, vec * sizeof(T)) || !aligned_to(p1, vec * sizeof(T))))
         vec /= 2;
     d.VEC = vec;
-    const int64_t nvec = (kt + vec - 1) / vec;  // column vectors per row of one tile
+    const int64_t nvec = (K + vec - 1) / vec;  // column vectors per row
     int g = pow2_floor(std::min(std::max(s.threads_per_row, 4), 32));
     g = std::max(4, std::min(g, pow2_ceil(nvec)));
     d.G = g;
     const int64_t per_lane = (nvec + g - 1) / g;
     d.NCV = per_lane <= 1 ? 1 : (per_lane <= 2 ? 2 : 4);
     // SpMM covers at most G*VEC*NCV columns per launch (its accumulators live in
-    // registers); SDDMM loops over its tile inside the kernel
-    d.ktile = is_spmm ? std::min<int64_t>(kt, (int64_t)g * vec * d.NCV) : kt;
+    // registers); SDDMM loops over all K columns inside the kernel
+    d.ktile = is_spmm ? std::min<int64_t>(K, (int64_t)g * vec * d.NCV) : K;
     d.U = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
     d.block = (s.block_size >= 512) ? 512 : (s.block_size >= 256 ? 256 : 128);
-    d.merge = (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM);
+    d.merge = (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM || s.split == TG_SPLIT_BLOCK);
     d.S = s.chunk_nnz > 0 ? s.chunk_nnz : default_dense_chunk(nnz, is_spmm);
     return d;
 }
@@ -166,10 +140,14 @@ bool dense_dispatch(const DenseChoice& d, bool sp, const DenseArgs<T>& a, cudaSt
     return false;
 }
 
+// SpMM with TG_SPLIT_BLOCK: the group plan (one flag byte per group of kGroupRows rows).
+inline bool block_split(const tg_sched& s, bool is_spmm) { return is_spmm && s.split == TG_SPLIT_BLOCK; }
+
 template <typename T>
 size_t dense_ws_bytes(int64_t rows, int64_t nnz, int64_t K, const tg_sched& s, bool is_spmm) {
-    (void)rows;
-    if ((s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_STREAM) || nnz <= 0 || K <= 0) return 0;
+    if (block_split(s, is_spmm)) return rows > 0 ? align256((size_t)ceil_div(rows, kGroupRows)) : 0;
+    if ((s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_STREAM && s.split != TG_SPLIT_BLOCK) || nnz <= 0 || K <= 0)
+        return 0;
     // alignment does not change the partial width's upper bound: size for the widest tile
     const DenseChoice d = choose_dense<T>(s, K, is_spmm, nullptr, nullptr, nnz);
     const int64_t nchunks = ceil_div(nnz, d.S);
@@ -177,20 +155,17 @@ size_t dense_ws_bytes(int64_t rows, int64_t nnz, int64_t K, const tg_sched& s, b
     return split_ws_bytes(nchunks, width, sizeof(T));
 }
 
-// One launch per column tile [k0, k0 + ktile).  SpMM writes C's columns of the tile;
-// SDDMM accumulates each nonzero's dot product over the tiles in order (kPass*).
+// SpMM: one launch per slab of G*VEC*NCV columns (the accumulators of a lane group
+// cover that many); SDDMM: one launch.
 template <typename T>
 int launch_tiles(const DenseChoice& d, bool is_spmm, const DenseArgs<T>& a, const T* B, const T* U, T* C, int64_t K,
                  cudaStream_t st) {
-    const int64_t ntiles = (K + d.ktile - 1) / d.ktile;
-    for (int64_t ti = 0; ti < ntiles; ++ti) {
-        const int64_t k0 = ti * d.ktile;
+    for (int64_t k0 = 0; k0 < (is_spmm ? K : 1); k0 += d.ktile) {
         DenseArgs<T> t = a;
-        t.B = B + k0;
-        t.U = is_spmm ? U : U + k0;
-        t.C = is_spmm ? C + k0 : C;
-        t.kt = std::min(d.ktile, K - k0);
-        t.pass = ntiles == 1 ? kPassOnly : (ti == 0 ? kPassFirst : (ti == ntiles - 1 ? kPassLast : kPassMid));
+        t.B = B + (is_spmm ? k0 : 0);
+        t.U = U;
+        t.C = C + (is_spmm ? k0 : 0);
+        t.kt = is_spmm ? std::min(d.ktile, K - k0) : K;
         if (!dense_dispatch<T>(d, is_spmm, t, st))
             return set_error(TG_EUNSUPPORTED, "no %s instance for G=%d VEC=%d NCV=%d U=%d", is_spmm ? "spmm" : "sddmm",
                              d.G, d.VEC, d.NCV, d.U);
@@ -200,13 +175,55 @@ int launch_tiles(const DenseChoice& d, bool is_spmm, const DenseArgs<T>& a, cons
     return TG_OK;
 }
 
+// SpMM over row groups (TG_SPLIT_BLOCK): plan unless reused, then one launch (the
+// warps loop over K in slices of 32*VEC columns).
+template <typename T>
+int spmm_groups_run(const tg_csr& A, const T* B, T* C, int64_t K, const tg_sched& s, void* ws, size_t ws_bytes,
+                    cudaStream_t st) {
+    const int64_t ngroups = ceil_div(A.rows, kGroupRows);
+    const size_t need = align256((size_t)ngroups);
+    if (ws == nullptr || ws_bytes < need)
+        return set_error(TG_ENOMEM, "spmm block split needs %zu workspace bytes, got %zu", need, ws_bytes);
+    uint8_t* flag = static_cast<uint8_t*>(ws);
+    const int64_t warps_per_cta = 256 / kWarp;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(ngroups, warps_per_cta), 148 * 32));
+    if (!(s.flags & TG_FLAG_REUSE_PLAN)) {
+        group_plan_kernel<kGroupRows><<<(unsigned)blocks, 256, 0, st>>>(A.indptr, A.indices, A.rows, ngroups, flag);
+        const int rc = check_launch("group_plan_kernel");
+        if (rc != TG_OK) return rc;
+    }
+    const int vmax = sizeof(T) == 4 ? 4 : 2;
+    int vec = vmax;
+    while (vec > 1 && (K % vec != 0 || !aligned_to(B, vec * sizeof(T)) || !aligned_to(C, vec * sizeof(T)))) vec /= 2;
+    DenseArgs<T> a{};
+    a.indptr = A.indptr;
+    a.indices = A.indices;
+    a.data = static_cast<const T*>(A.data);
+    a.rows = A.rows;
+    a.nnz = A.nnz;
+    a.ld = K;
+    a.row_limit = (s.flags & TG_FLAG_INJECT_BUG) ? A.rows - 1 : A.rows;
+    a.B = B;
+    a.C = C;
+    a.kt = K;
+    if (vec == 4) {
+        if constexpr (sizeof(T) == 4) spmm_group_kernel<T, 4, 4><<<(unsigned)blocks, 256, 0, st>>>(a, flag, ngroups);
+    } else if (vec == 2) {
+        spmm_group_kernel<T, 2, 4><<<(unsigned)blocks, 256, 0, st>>>(a, flag, ngroups);
+    } else {
+        spmm_group_kernel<T, 1, 4><<<(unsigned)blocks, 256, 0, st>>>(a, flag, ngroups);
+    }
+    return check_launch("spmm_group_kernel");
+}
+
 // C = A * B (SpMM) or out = A .* (U V^T) on A's pattern (SDDMM, B = V).
 template <typename T>
 int dense_run(bool is_spmm, const tg_csr& A, const T* B, const T* U, T* C, int64_t K, const tg_sched& s, void* ws,
               size_t ws_bytes, cudaStream_t st) {
     if (K <= 0) return set_error(TG_EINVAL, "dense width K must be positive (got %lld)", (long long)K);
     if (A.rows == 0) return TG_OK;
-    const DenseChoice d = choose_dense<T>(s, K, is_spmm, B, is_spmm ? (const void*)C : (const void*)U, A.nnz, A.cols);
+    if (block_split(s, is_spmm)) return spmm_groups_run<T>(A, B, C, K, s, ws, ws_bytes, st);
+    const DenseChoice d = choose_dense<T>(s, K, is_spmm, B, is_spmm ? (const void*)C : (const void*)U, A.nnz);
     DenseArgs<T> a{};
     a.indptr = A.indptr;
     a.indices = A.indices;

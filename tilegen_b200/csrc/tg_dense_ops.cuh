@@ -16,11 +16,7 @@
 // SpMM writes C (no pre-zeroing needed); rows split across chunks are reduced with the
 // deterministic last-arriver protocol using K-wide partial rows.  SDDMM writes one value
 // per nonzero in A's order, so the output pattern is A's by construction.
-//
-// Column tiling (host side, tg_dense_host.cuh): when the gathered operand (B or V) is
-// larger than an L2 budget, the call is split into launches over column tiles whose
-// slab of it fits in L2, so each dense row is fetched from DRAM about once instead of
-// once per nonzero that touches it; the CSR stream is re-read per tile.
+
 #pragma once
 
 #include "tg_split.cuh"
@@ -43,18 +39,11 @@ struct DenseArgs {
     int64_t S;       // merge: nonzeros per chunk
     int64_t nunits;  // rows (rowwise) or chunks (merge)
     int64_t row_limit;
-    int pass;        // SDDMM column tile: kPassOnly / kPassFirst / kPassMid / kPassLast
     const int64_t* own_first;
     int* cnt;
     T* head;
     T* tail;
 };
-
-// SDDMM over column tiles.  Each nonzero's dot product is accumulated in out[p] across
-// the launches, one tile after the other (a fixed order), and A's value is applied by
-// the last one: only tile: out = a * dot; first: out = dot; middle: out += dot; last:
-// out = a * (out + dot).
-constexpr int kPassOnly = 0, kPassFirst = 1, kPassMid = 2, kPassLast = 3;
 
 template <int G>
 __device__ __forceinline__ unsigned group_mask() {
@@ -266,7 +255,7 @@ __global__ void __launch_bounds__(512) sddmm_kernel(DenseArgs<T> a) {
                 crow[u] = r;
                 if (q < ce) {
                     cidx[u] = ld_stream(a.indices + q, ps);
-                    if (a.pass == kPassOnly || a.pass == kPassLast) cval[u] = ld_stream(a.data + q, ps);
+                    cval[u] = ld_stream(a.data + q, ps);
                     if constexpr (MERGE) {
                         while (nxt <= q) {
                             ++r;
@@ -296,15 +285,158 @@ __global__ void __launch_bounds__(512) sddmm_kernel(DenseArgs<T> a) {
             for (int u = 0; u < U; ++u) {
                 T d = group_sum<G>(dot[u].get(), gmask);
                 const int64_t q = q0 + u;
-                if (lane == (u % G) && q < ce && crow[u] < a.row_limit) {
-                    if (a.pass == kPassOnly) {
-                        a.C[q] = cval[u] * d;
-                    } else if (a.pass == kPassFirst) {
-                        a.C[q] = d;
-                    } else if (a.pass == kPassMid) {
-                        a.C[q] += d;
-                    } else {
-                        a.C[q] = cval[u] * (a.C[q] + d);
+                if (lane == (u % G) && q < ce && crow[u] < a.row_limit) a.C[q] = cval[u] * d;
+            }
+        }
+    }
+}
+
+}  // namespace tg
+
+namespace tg {
+
+// ------------------------------------------------------------------ row groups
+// Block-structured matrices (the reference corpus's `blocked` class, dense 8x8 blocks,
+// tilegen/matrices.py:135-161; BSR in tilegen/ir.py:101) store, in CSR, runs of
+// consecutive rows with identical column lists.  With TG_SPLIT_BLOCK the SpMM works on
+// GROUPS of kGroupRows consecutive rows: a plan pass flags every group whose rows share
+// one column list, and for a flagged group one warp gathers each dense row B[j, :] ONCE
+// and applies it to all of the group's rows (kGroupRows x fewer gathers); other groups
+// are done row by row by the same warp.  Each row is summed over its nonzeros in index
+// order, as in the rowwise kernel, so the results are the same.
+constexpr int kGroupRows = 8;
+
+// flag[g] = 1 when rows [g*R, g*R + R) all exist and have the same column list.  One
+// warp per group; lanes stride over the positions.
+template <int R>
+__global__ void __launch_bounds__(256) group_plan_kernel(const int64_t* __restrict__ indptr,
+                                                         const int64_t* __restrict__ indices, int64_t rows,
+                                                         int64_t ngroups, uint8_t* __restrict__ flag) {
+    const int lane = threadIdx.x % kWarp;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) / kWarp;
+    for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / kWarp; g < ngroups; g += nw) {
+        const int64_t r0 = g * R;
+        bool same = r0 + R <= rows;
+        if (same) {
+            const int64_t p0 = indptr[r0];
+            const int64_t len = indptr[r0 + 1] - p0;
+            for (int r = 1; r < R && same; ++r) {
+                const int64_t pr = indptr[r0 + r];
+                if (indptr[r0 + r + 1] - pr != len) {
+                    same = false;
+                    break;
+                }
+                bool ok = true;
+                for (int64_t q = lane; q < len; q += kWarp) ok &= (indices[p0 + q] == indices[pr + q]);
+                same = __all_sync(kFull, ok);
+            }
+        }
+        if (lane == 0) flag[g] = same ? 1 : 0;
+    }
+}
+
+// One warp per group, grid-stride.  Lane l owns the VEC columns s + l*VEC of each 32*VEC
+// column slice s of this launch's tile.  Positions are read 32 at a time (one coalesced
+// load of indices and of each row's values per 32 positions) and handed out by shuffles;
+// UG gathers are in flight per lane.
+template <typename T, int VEC, int UG>
+__global__ void __launch_bounds__(256) spmm_group_kernel(DenseArgs<T> a, const uint8_t* __restrict__ flag,
+                                                         int64_t ngroups) {
+    constexpr int R = kGroupRows;
+    const int lane = threadIdx.x % kWarp;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) / kWarp;
+    const uint64_t ps = policy_evict_first();
+    const uint64_t pg = policy_evict_last();
+    for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / kWarp; g < ngroups; g += nw) {
+        const int64_t r0 = g * R;
+        const bool grouped = flag[g] != 0;
+        const int nrows = (int)min((int64_t)R, a.rows - r0);
+        for (int64_t s0 = 0; s0 < a.kt; s0 += (int64_t)kWarp * VEC) {
+            const int64_t col = s0 + (int64_t)lane * VEC;
+            const bool live = col < a.kt;
+            if (grouped) {
+                int64_t base[R];
+#pragma unroll
+                for (int r = 0; r < R; ++r) base[r] = a.indptr[r0 + r];
+                const int64_t len = a.indptr[r0 + 1] - base[0];
+                Sum<T> acc[R][VEC];
+                for (int64_t p0 = 0; p0 < len; p0 += kWarp) {
+                    const int n = (int)min((int64_t)kWarp, len - p0);
+                    int64_t myidx = 0;
+                    T myval[R];
+                    if (lane < n) myidx = ld_stream(a.indices + base[0] + p0 + lane, ps);
+#pragma unroll
+                    for (int r = 0; r < R; ++r) myval[r] = lane < n ? ld_stream(a.data + base[r] + p0 + lane, ps) : T(0);
+                    for (int j0 = 0; j0 < n; j0 += UG) {
+                        Vec<T, VEC> b[UG];
+#pragma unroll
+                        for (int u = 0; u < UG; ++u) {
+                            const int64_t c = __shfl_sync(kFull, myidx, (j0 + u) & 31);
+#pragma unroll
+                            for (int e = 0; e < VEC; ++e) b[u].v[e] = T(0);
+                            if (live && j0 + u < n) b[u] = ld_gather_vec<T, VEC>(a.B + c * a.ld + col, pg);
+                        }
+#pragma unroll
+                        for (int u = 0; u < UG; ++u) {
+                            if (j0 + u < n) {  // warp-uniform
+#pragma unroll
+                                for (int r = 0; r < R; ++r) {
+                                    const T v = __shfl_sync(kFull, myval[r], j0 + u);
+#pragma unroll
+                                    for (int e = 0; e < VEC; ++e) acc[r][e].mad(v, b[u].v[e]);
+                                }
+                            }
+                        }
+                    }
+                }
+                if (live) {
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        if (r0 + r < a.row_limit) {
+                            Vec<T, VEC> o;
+#pragma unroll
+                            for (int e = 0; e < VEC; ++e) o.v[e] = acc[r][e].get();
+                            st_vec<T, VEC>(a.C + (r0 + r) * a.ld + col, o);
+                        }
+                    }
+                }
+            } else {
+                for (int r = 0; r < nrows; ++r) {
+                    const int64_t rr = r0 + r;
+                    const int64_t pb = a.indptr[rr], pe = a.indptr[rr + 1];
+                    Sum<T> acc[VEC];
+                    for (int64_t p0 = pb; p0 < pe; p0 += kWarp) {
+                        const int n = (int)min((int64_t)kWarp, pe - p0);
+                        int64_t myidx = 0;
+                        T myval = T(0);
+                        if (lane < n) {
+                            myidx = ld_stream(a.indices + p0 + lane, ps);
+                            myval = ld_stream(a.data + p0 + lane, ps);
+                        }
+                        for (int j0 = 0; j0 < n; j0 += UG) {
+                            Vec<T, VEC> b[UG];
+#pragma unroll
+                            for (int u = 0; u < UG; ++u) {
+                                const int64_t c = __shfl_sync(kFull, myidx, (j0 + u) & 31);
+#pragma unroll
+                                for (int e = 0; e < VEC; ++e) b[u].v[e] = T(0);
+                                if (live && j0 + u < n) b[u] = ld_gather_vec<T, VEC>(a.B + c * a.ld + col, pg);
+                            }
+#pragma unroll
+                            for (int u = 0; u < UG; ++u) {
+                                if (j0 + u < n) {
+                                    const T v = __shfl_sync(kFull, myval, j0 + u);
+#pragma unroll
+                                    for (int e = 0; e < VEC; ++e) acc[e].mad(v, b[u].v[e]);
+                                }
+                            }
+                        }
+                    }
+                    if (live && rr < a.row_limit) {
+                        Vec<T, VEC> o;
+#pragma unroll
+                        for (int e = 0; e < VEC; ++e) o.v[e] = acc[e].get();
+                        st_vec<T, VEC>(a.C + rr * a.ld + col, o);
                     }
                 }
             }

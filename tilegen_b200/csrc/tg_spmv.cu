@@ -301,7 +301,7 @@ size_t spmv_ws_bytes(int64_t rows, int64_t nnz, const tg_sched& s, size_t elem) 
     if (s.split == TG_SPLIT_STREAM && nnz > 0)
         return std::max(stream_ws_bytes(nnz, s, elem),
                         split_ws_bytes(ceil_div(nnz, merge_chunk_nnz(merge_block(s))), 1, elem));
-    if (s.split != TG_SPLIT_MERGE || nnz <= 0) return 0;
+    if ((s.split != TG_SPLIT_MERGE && s.split != TG_SPLIT_BLOCK) || nnz <= 0) return 0;
     const int64_t S = merge_chunk_nnz(merge_block(s));
     return split_ws_bytes(ceil_div(nnz, S), 1, elem);
 }
@@ -332,8 +332,9 @@ int spmv_run(const tg_csr& A, const T* x, T* y, const Epi<T, AXPY>& epi, const t
             return stream_run<T, kStreamPlain>(A, x, y, nullptr, T(0), T(0), 1, 0, s, ws, ws_bytes, st);
         }
     }
-    if (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM) {
+    if (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM || s.split == TG_SPLIT_BLOCK) {
         // stream needs 16-byte aligned operands; the merge split handles any alignment
+        // (the block split is an SpMM mapping: SpMV takes the merge split for it)
         const int B = merge_block(s);
         const int64_t S = merge_chunk_nnz(B);
         const int64_t nchunks = ceil_div(A.nnz, S);

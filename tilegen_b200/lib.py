@@ -28,6 +28,7 @@ TG_SPLIT_ROWWISE = 0
 TG_SPLIT_MERGE = 1
 TG_SPLIT_AUTO = 2
 TG_SPLIT_STREAM = 3
+TG_SPLIT_BLOCK = 4
 
 TG_FLAG_BOUNDS_CHECK = 1
 TG_FLAG_INJECT_BUG = 2
