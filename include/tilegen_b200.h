@@ -231,6 +231,15 @@ TG_API int tg_ipc_get_handle(const void* ptr, void* handle /* 64 bytes */);
 TG_API int tg_ipc_open(const void* handle /* 64 bytes */, void** ptr);
 TG_API int tg_ipc_close(void* ptr);
 
+/* ------------------------------------------- column-locality reordering (new) */
+/* Reverse Cuthill-McKee order of a square matrix (no counterpart in the reference; an
+ * optional preprocessing pass).  HOST arrays: indptr[n+1], indices[indptr[n]] in [0, n).
+ * perm[new] = old, a permutation of 0..n-1 computed on the symmetrised pattern
+ * (A + A^T).  Applying it as A' = P A P^T, x' = P x (B' = P B, V' = P V, U' = P U) gives
+ * y' = P y: rows that share columns get nearby numbers, which raises the L2 hit rate of
+ * the gathers where the pattern has such structure. */
+TG_API int tg_rcm_order(int64_t n, const int64_t* indptr, const int64_t* indices, int64_t* perm);
+
 /* ----------------------------------------------- SpMV that allocates nothing */
 /* No counterpart in the reference.  y = A x (fp64, merge split) for callers that can
  * pass only inputs and outputs -- a host that owns the whole GPU memory pool, or a path

@@ -139,6 +139,7 @@ SIGNATURES = {
     "tg_ipc_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "tg_ipc_close": (ctypes.c_int, [_P]),
     "tg_spmv_f64_noalloc": (ctypes.c_int, [_CP, _P, _P, _SP, _P]),
+    "tg_rcm_order": (ctypes.c_int, [_I64, _P, _P, _P]),
     "launch_spmv": (None, [_P, _P, _P, _P, _P, _I64, _I64, _I64]),
     "launch_spmm": (None, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64]),
     "launch_sddmm": (None, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64]),
