@@ -48,7 +48,7 @@ X0_SEED = 7
 ITERS = 20
 FALLBACK_HBM_GBS = 6650.0
 
-WORKLOADS = ("c4", "c1", "c2", "c3", "c5-spmm", "c5-sddmm", "c5-spmm-rcm")
+WORKLOADS = ("c4", "c1", "c2", "c3", "c5-spmm", "c5-sddmm", "c5-spmm-rcm", "blocked-spmm")
 # Default schedule per workload: the fastest measured in the schedule sweeps on a B200.
 SCHEDULES = {
     "c4": {"split": "rowwise", "tpr": 4, "unroll": 2, "vec": 2, "block": 256},
@@ -58,6 +58,7 @@ SCHEDULES = {
     "c5-spmm": {"split": "merge", "tpr": 32, "unroll": 4, "vec": 4, "block": 128},
     "c5-sddmm": {"split": "merge", "tpr": 8, "unroll": 1, "vec": 4, "block": 128},
     "c5-spmm-rcm": {"split": "merge", "tpr": 32, "unroll": 4, "vec": 4, "block": 128},
+    "blocked-spmm": {"split": "block", "tpr": 32, "unroll": 4, "vec": 4, "block": 256},
 }
 
 
@@ -73,7 +74,7 @@ def parse():
     ap.add_argument("--workload", choices=WORKLOADS, default="c4",
                     help="c4: the power-iteration headline (default); c1/c2/c3: one SpMV per step; "
                          "c5-spmm / c5-sddmm: one SpMM (K=128) / SDDMM (K=64) per step, fp32")
-    ap.add_argument("--split", choices=["stream", "rowwise", "merge"], default=None)
+    ap.add_argument("--split", choices=["stream", "rowwise", "merge", "block"], default=None)
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: fused SpMV + peer-memory push (p2p) or NCCL all-gather")
     ap.add_argument("--tpr", type=int, default=None)
@@ -274,29 +275,31 @@ def workload_config(n: int, world: int, exchange: str = "p2p"):
 
 
 # ----------------------------------------------------------------------------- C1-C3, C5
-K_DENSE = {"c5-spmm": 128, "c5-sddmm": 64, "c5-spmm-rcm": 128}
+K_DENSE = {"c5-spmm": 128, "c5-sddmm": 64, "c5-spmm-rcm": 128, "blocked-spmm": 128}
+SPMM_WORKLOADS = ("c5-spmm", "c5-spmm-rcm", "blocked-spmm")
+FP32_WORKLOADS = ("c5-spmm", "c5-sddmm", "c5-spmm-rcm", "blocked-spmm")
 INPUT_SEED = 11
 
 
 def matrix_kernel(workload: str) -> str:
-    return {"c5-spmm": "spmm", "c5-sddmm": "sddmm", "c5-spmm-rcm": "spmm"}.get(workload, "spmv")
+    return {"c5-sddmm": "sddmm"}.get(workload, "spmm" if workload in SPMM_WORKLOADS else "spmv")
 
 
 def matrix_bytes(workload: str, A) -> int:
     """Compulsory bytes of one call on the whole matrix: indptr + indices + values + dense
     inputs + outputs, each once (8-byte indices; fp64 for SpMV, fp32 for C5)."""
     M, N, nnz = A.rows, A.cols, A.nnz
-    if workload.startswith("c5"):
+    if workload in FP32_WORKLOADS:
         K = K_DENSE[workload]
         base = 8 * (M + 1) + 12 * nnz
-        if workload in ("c5-spmm", "c5-spmm-rcm"):
+        if workload in SPMM_WORKLOADS:
             return base + 4 * N * K + 4 * M * K
         return base + 4 * M * K + 4 * N * K + 4 * nnz
     return spmv_bytes(M, N, nnz)
 
 
 def matrix_flops(workload: str, A) -> float:
-    if workload.startswith("c5"):
+    if workload in FP32_WORKLOADS:
         return 2.0 * A.nnz * K_DENSE[workload] + (A.nnz if workload == "c5-sddmm" else 0)
     return 2.0 * A.nnz
 
@@ -305,7 +308,7 @@ def matrix_inputs(workload: str, A):
     """Seeded U(-1,1) dense operands: x (fp64) for SpMV, B (N x 128) or U (M x 64),
     V (N x 64) in fp32 for C5."""
     rng = np.random.default_rng([INPUT_SEED, 0])
-    if workload in ("c5-spmm", "c5-spmm-rcm"):
+    if workload in SPMM_WORKLOADS:
         return {"B": rng.uniform(-1.0, 1.0, size=(A.cols, 128)).astype(np.float32)}
     if workload == "c5-sddmm":
         U = rng.uniform(-1.0, 1.0, size=(A.rows, 64)).astype(np.float32)
@@ -329,7 +332,9 @@ def matrix_config(workload: str, A, world: int, flush: bool):
             "c5-spmm": "C5 SpMM: power_law 1000000^2 (Zipf(2), mean 16) x dense 1000000x128, fp32",
             "c5-sddmm": "C5 SDDMM: power_law 1000000^2 (Zipf(2), mean 16) pattern, U,V 1000000x64, fp32",
             "c5-spmm-rcm": "C5 SpMM after reverse Cuthill-McKee reordering (labelled configuration: A' = P A P^T, "
-                           "B' = P B, C' = P C; changes the input order)"}[workload]
+                           "B' = P B, C' = P C; changes the input order)",
+            "blocked-spmm": "SpMM K=128 fp32 on the reference corpus's blocked class (100000^2, dense 8x8 blocks, "
+                            "2 per block row; labelled configuration for block-structured matrices)"}[workload]
     return {"workload": desc, "rows": A.rows, "cols": A.cols, "nnz": A.nnz,
             "max_row_nnz": int(np.diff(A.indptr).max()) if A.rows else 0,
             "parallelism": "single GPU" if world == 1 else
@@ -367,7 +372,7 @@ def cpu_matrix_caller(workload: str, A, inputs):
     from oracle import oracle as O
 
     kernel = matrix_kernel(workload)
-    dtype = "f32" if workload.startswith("c5") else "f64"
+    dtype = "f32" if workload in FP32_WORKLOADS else "f64"
     M, N, nnz = A.rows, A.cols, A.nnz
     ip, ix = A.indptr, A.indices
     d = A.data.astype(np.float32) if dtype == "f32" else A.data
@@ -420,7 +425,8 @@ def run_matrix_reference(args, rank: int, world: int):
         return 0
     from tilegen_b200 import matrices as Mx
 
-    A = Mx.baseline_matrix("c5" if args.workload.startswith("c5") else args.workload)
+    A = (Mx.make_matrix("blocked") if args.workload == "blocked-spmm" else
+         Mx.baseline_matrix("c5" if args.workload.startswith("c5") else args.workload))
     inputs = matrix_inputs(args.workload, A)
     call, kind, desc, threads = cpu_matrix_caller(args.workload, A, inputs)
     if call is None:
@@ -438,7 +444,7 @@ def run_matrix_reference(args, rank: int, world: int):
     line = {"impl": "reference", "metric": "effective_hbm_gbs_" + matrix_kernel(args.workload), "value": round(gbs, 3),
             "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(sec * 1e3, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32" if args.workload.startswith("c5") else "f64", "data": "synthetic (seeded generators)",
+            "dtype": "f32" if args.workload in FP32_WORKLOADS else "f64", "data": "synthetic (seeded generators)",
             "config": matrix_config(args.workload, A, world, None),
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
                              "sample": "one whole-matrix call per step", "impl": desc},
@@ -452,7 +458,8 @@ def make_sched(split: str, tpr: int, unroll: int, vec: int, block: int):
 
     sch = lib.default_schedule()
     sch.threads_per_row, sch.unroll, sch.vector_width, sch.block_size, sch.tile = tpr, unroll, vec, block, 32
-    sch.split = {"rowwise": lib.TG_SPLIT_ROWWISE, "merge": lib.TG_SPLIT_MERGE, "stream": lib.TG_SPLIT_STREAM}[split]
+    sch.split = {"rowwise": lib.TG_SPLIT_ROWWISE, "merge": lib.TG_SPLIT_MERGE, "stream": lib.TG_SPLIT_STREAM,
+                 "block": lib.TG_SPLIT_BLOCK}[split]
     lib.validate_schedule(sch)
     return sch
 
@@ -471,8 +478,8 @@ def measure_matrix(wl: str, sched: dict, steps: int, warmup: int, rank: int, wor
 
     L = lib.load()
     kernel = matrix_kernel(wl)
-    c5 = wl.startswith("c5")
-    A = Mx.baseline_matrix("c5" if c5 else wl)
+    c5 = wl in FP32_WORKLOADS
+    A = Mx.make_matrix("blocked") if wl == "blocked-spmm" else Mx.baseline_matrix("c5" if wl.startswith("c5") else wl)
     inputs = matrix_inputs(wl, A)
     reorder = None
     if wl.endswith("-rcm"):
@@ -521,7 +528,24 @@ def measure_matrix(wl: str, sched: dict, steps: int, warmup: int, rank: int, wor
             step = lambda: D.spmv(Ad, d_in["x"], out, sched=sch)  # noqa: E731
     elif kernel == "spmm":
         out = torch.empty((S.rows, 128), dtype=dt, device=dev)
-        step = lambda: D.spmm(Ad, d_in["B"], out, sched=sch)  # noqa: E731
+        if sched["split"] == "block":
+            # the row-group flags (the plan) are computed by the first call and reused
+            ws = torch.zeros(max(1, int(L.tg_spmm_workspace_bytes(S.rows, S.nnz, 128, ctypes.byref(sch)))),
+                             dtype=torch.uint8, device=dev)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            D.spmm(Ad, d_in["B"], out, sched=sch, workspace=ws)  # planning call
+            e1.record()
+            torch.cuda.synchronize(dev)
+            plan = {"first_call_ms": round(e0.elapsed_time(e1), 5),
+                    "note": "row-group flags computed by the first call, reused by every timed call "
+                            "(TG_FLAG_REUSE_PLAN)"}
+            sch_r = make_sched(sched["split"], sched["tpr"], sched["unroll"], sched["vec"], sched["block"])
+            sch_r.flags |= lib.TG_FLAG_REUSE_PLAN
+            step = lambda: D.spmm(Ad, d_in["B"], out, sched=sch_r, workspace=ws)  # noqa: E731
+        else:
+            step = lambda: D.spmm(Ad, d_in["B"], out, sched=sch)  # noqa: E731
     else:
         out = torch.empty(S.nnz, dtype=dt, device=dev)
         step = lambda: D.sddmm(Ad, d_in["U"], d_in["V"], out, sched=sch)  # noqa: E731
@@ -641,7 +665,7 @@ def warm_graph_ms(step, dev, calls: int = 20, replays: int = 5):
 
 def matrix_kernel_name(kernel: str, split: str) -> str:
     return {"spmv": "spmv_rowwise_kernel" if split == "rowwise" else "spmv_merge_kernel",
-            "spmm": "spmm kernel", "sddmm": "sddmm kernel"}[kernel]
+            "spmm": "spmm_group_kernel" if split == "block" else "spmm kernel", "sddmm": "sddmm kernel"}[kernel]
 
 
 def summarise_matrix(rec, ms_step: float, world: int, peak: float):
@@ -761,7 +785,7 @@ def cusparse_compare(workload: str, Ad, d_in, flush, steps: int, total_bytes: in
 
     try:
         Sp = torch.sparse_csr_tensor(Ad.indptr, Ad.indices, Ad.data, size=(Ad.rows, Ad.cols))
-        if workload in ("c5-spmm", "c5-spmm-rcm"):
+        if workload in SPMM_WORKLOADS:
             fn = lambda: torch.sparse.mm(Sp, d_in["B"])  # noqa: E731
             op = "torch.sparse.mm (cusparseSpMM)"
         elif workload == "c5-sddmm":
@@ -967,7 +991,7 @@ def main():
     workloads = {}
     if not args.no_workloads:
         peak, _ = measured_peaks()
-        for wl in ("c1", "c2", "c3", "c5-spmm", "c5-sddmm") + (("c5-spmm-rcm",) if world == 1 else ()):
+        for wl in ("c1", "c2", "c3", "c5-spmm", "c5-sddmm") + (("c5-spmm-rcm", "blocked-spmm") if world == 1 else ()):
             rec = measure_matrix(wl, SCHEDULES[wl], args.steps, args.warmup, rank, world, dev, barrier, 2,
                                  want_cpu=(world == 1 and rank == 0 and not args.no_cpu_baseline),
                                  want_cusparse=(world == 1 and not args.no_cusparse), sample_clocks=False)

@@ -35,15 +35,13 @@ def test_compulsory_bytes(bench):
     assert bench.matrix_bytes("c5-sddmm", A) == 8 * 5 + 12 * 6 + 4 * 4 * 64 * 2 + 4 * 6
     assert bench.spmv_bytes(8_000_000, 8_000_000, 256_000_000) == 4_288_000_008
     assert bench.matrix_flops("c5-spmm", A) == 2.0 * 6 * 128
+    assert bench.matrix_bytes("blocked-spmm", A) == bench.matrix_bytes("c5-spmm", A)
+    assert bench.matrix_kernel("blocked-spmm") == "spmm" and bench.matrix_kernel("c5-sddmm") == "sddmm"
 
 
 def test_default_schedules_are_valid(bench):
-    split = {"rowwise": lib.TG_SPLIT_ROWWISE, "merge": lib.TG_SPLIT_MERGE, "stream": lib.TG_SPLIT_STREAM}
     for wl, d in bench.SCHEDULES.items():
-        s = lib.default_schedule()
-        s.threads_per_row, s.unroll, s.vector_width, s.block_size = d["tpr"], d["unroll"], d["vec"], d["block"]
-        s.split = split[d["split"]]
-        lib.validate_schedule(s)  # raises on a schedule the library would reject
+        bench.make_sched(d["split"], d["tpr"], d["unroll"], d["vec"], d["block"])  # raises on a rejected schedule
     assert set(bench.SCHEDULES) == set(bench.WORKLOADS)
 
 
