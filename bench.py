@@ -932,7 +932,7 @@ def main():
 
     def probe():
         bench_probe.gather_probe_f64(pi.indices.data_ptr(), pi.nnz, pi.x[0].data_ptr(), probe_out.data_ptr(),
-                                     stream.cuda_stream)
+                                     stream.cuda_stream, index32=pi.index32)
 
     def ev():
         return torch.cuda.Event(enable_timing=True)

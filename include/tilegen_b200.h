@@ -69,6 +69,9 @@ typedef void* tg_stream_t;
 /* flags */
 #define TG_FLAG_BOUNDS_CHECK 1u /* validate indptr/indices on the device; TG_EBOUNDS on error */
 #define TG_FLAG_INJECT_BUG 2u   /* deliberately skip the last row (harness self-test) */
+#define TG_FLAG_INDEX32 8u      /* power steps (tg_power_step_f64, tg_power_step_p2p_f64):
+                                   A.indices points to int32 column indices (renumbered by
+                                   tg_renumber_columns_i32); rowwise split, no bounds check */
 #define TG_FLAG_REUSE_PLAN 4u   /* SpMV merge / stream and SpMM block splits: the workspace
                                    already holds this matrix's plan (partition or row-group
                                    flags) from an earlier call with the same A and schedule;
@@ -181,6 +184,11 @@ TG_API size_t tg_power_workspace_bytes(int64_t nnz, const tg_sched* s);
  * `stride`; the indices must lie in [0, bounds[nparts]).  out may equal indices. */
 TG_API int tg_renumber_columns(const int64_t* indices, int64_t* out, int64_t nnz, const int64_t* bounds,
                                int32_t nparts, int64_t stride, tg_stream_t stream);
+/* The same renumbering written as int32 (the padded layout nparts * stride must be below
+ * 2^31): the power steps read it with TG_FLAG_INDEX32, 12 bytes of CSR stream per nonzero
+ * instead of 16. */
+TG_API int tg_renumber_columns_i32(const int64_t* indices, int32_t* out, int64_t nnz, const int64_t* bounds,
+                                   int32_t nparts, int64_t stride, tg_stream_t stream);
 /* y[0..rows) = A x / sqrt(sum of the nparts slots of x); y[stride-1] = sum(y^2). */
 TG_API int tg_power_step_f64(const tg_csr* A, const double* x, int32_t nparts, int64_t stride,
                              double* y, const tg_sched* s, void* workspace,

@@ -239,3 +239,63 @@ def test_renumber_columns_kernel_matches_host(parts):
     got = renumber_columns(torch.as_tensor(j, device="cuda"), bounds, stride).cpu().numpy()
     assert np.array_equal(got, want)
 
+
+
+@pytest.mark.parametrize("parts", [1, 3])
+def test_int32_indices_give_the_same_iterates(parts):
+    """The power step reading int32 renumbered indices (TG_FLAG_INDEX32, the default for
+    the rowwise split) does the same arithmetic as with int64 ones: identical iterates."""
+    A = M.baseline_matrix("c3", scale=0.3)
+    bounds = nnz_balanced_bounds(A.row_lengths(), parts)
+    dev = torch.device("cuda")
+    x0 = np.random.default_rng(12).uniform(-1, 1, A.rows)
+    outs = {}
+    for i32 in (False, True):
+        pis = []
+        for r in range(parts):
+            a, b = int(bounds[r]), int(bounds[r + 1])
+            sl = slice(int(A.indptr[a]), int(A.indptr[b]))
+            pis.append(PowerIteration(torch.as_tensor(A.indptr[a:b + 1] - A.indptr[a]).to(dev),
+                                      torch.as_tensor(A.indices[sl]).to(dev), torch.as_tensor(A.data[sl]).to(dev),
+                                      bounds, r, sched=_sched(4, 2, 2), exchange=lambda x: None, index32=i32))
+        assert all(p.index32 == i32 for p in pis)
+        assert all(p.indices.dtype == (torch.int32 if i32 else torch.int64) for p in pis)
+        stride = pis[0].stride
+        for r, pi in enumerate(pis):
+            pi.set_x0(torch.as_tensor(x0[bounds[r]:bounds[r + 1]]).to(dev))
+        cur = 0
+        for it in range(7):
+            for r in range(parts):  # emulated all-gather
+                src = pis[r].x[cur][r * stride:(r + 1) * stride]
+                for q in range(parts):
+                    if q != r:
+                        pis[q].x[cur][r * stride:(r + 1) * stride].copy_(src)
+            for pi in pis:
+                pi._step(pi.x[cur], pi.shard(pi.x[1 - cur]))
+            cur = 1 - cur
+        outs[i32] = np.concatenate([pi.x[cur][r * stride:r * stride + pi.rows].cpu().numpy()
+                                    for r, pi in enumerate(pis)])
+    assert np.array_equal(outs[False], outs[True])
+
+
+def test_int32_renumbering_and_flag_checks():
+    from tilegen_b200.power import padded_stride, renumber_columns
+
+    rng = np.random.default_rng(5)
+    n = 20011
+    bounds = nnz_balanced_bounds(rng.integers(0, 9, size=n), 4)
+    stride = padded_stride(bounds)
+    j = rng.integers(0, n, size=70001).astype(np.int64)
+    want = renumber_columns(j, bounds, stride)
+    got = renumber_columns(torch.as_tensor(j, device="cuda"), bounds, stride, index32=True)
+    assert got.dtype == torch.int32 and np.array_equal(got.cpu().numpy().astype(np.int64), want)
+    # only the power steps take 32-bit indices
+    from tilegen_b200 import device as D
+
+    m = M.baseline_matrix("c1", scale=0.01)
+    A = D.DeviceCSR.from_host(m, "cuda")
+    s = lib.default_schedule()
+    s.flags |= lib.TG_FLAG_INDEX32
+    with pytest.raises(lib.TgError) as ei:
+        D.spmv(A, torch.zeros(m.cols, dtype=torch.float64, device="cuda"), sched=s)
+    assert ei.value.status == lib.TG_EUNSUPPORTED

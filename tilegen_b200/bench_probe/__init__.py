@@ -19,15 +19,19 @@ def load() -> ctypes.CDLL:
         if not os.path.exists(PROBE_PATH):
             raise OSError("libtg_gather_probe.so not found at %s; run `python -m tilegen_b200.build`" % PROBE_PATH)
         L = ctypes.CDLL(PROBE_PATH)
-        fn = L.tg_gather_probe_f64
-        fn.restype = ctypes.c_int
-        fn.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        for name in ("tg_gather_probe_f64", "tg_gather_probe_i32_f64"):
+            fn = getattr(L, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         _probe = L
     return _probe
 
 
-def gather_probe_f64(indices_ptr: int, n: int, x_ptr: int, out_ptr: int, stream: int) -> None:
-    """*out += sum of x[indices[i]] for i < n, on `stream` (device pointers)."""
-    rc = load().tg_gather_probe_f64(indices_ptr, n, x_ptr, out_ptr, stream)
+def gather_probe_f64(indices_ptr: int, n: int, x_ptr: int, out_ptr: int, stream: int, index32: bool = False) -> None:
+    """*out += sum of x[indices[i]] for i < n, on `stream` (device pointers; int64 column
+    indices, or int32 with ``index32``)."""
+    L = load()
+    fn = L.tg_gather_probe_i32_f64 if index32 else L.tg_gather_probe_f64
+    rc = fn(indices_ptr, n, x_ptr, out_ptr, stream)
     if rc != 0:
         raise RuntimeError("tg_gather_probe_f64 failed with status %d" % rc)

@@ -14,6 +14,7 @@
 //
 //   int tg_gather_probe_f64(const int64_t* indices, int64_t n, const double* x, double* out,
 //                           void* stream);
+//   int tg_gather_probe_i32_f64(const int32_t* indices, ...);   (int32 column indices)
 // *out += sum of x[indices[i]], i < n (device pointers; *out zeroed by the caller).
 // Returns 0, -1 for a bad argument, -2 when the launch failed.
 #include <algorithm>
@@ -23,7 +24,8 @@
 namespace tg {
 namespace {
 
-__global__ void __launch_bounds__(256) gather_probe_kernel(const int64_t* __restrict__ idx, int64_t n,
+template <typename I>
+__global__ void __launch_bounds__(256) gather_probe_kernel(const I* __restrict__ idx, int64_t n,
                                                            const double* __restrict__ x, double* out) {
     const uint64_t ps = policy_evict_first();
     const uint64_t pg = policy_evict_last();
@@ -42,6 +44,16 @@ __global__ void __launch_bounds__(256) gather_probe_kernel(const int64_t* __rest
     if ((threadIdx.x % kWarp) == 0) atomicAdd(out, acc);
 }
 
+template <typename I>
+int probe_run(const I* indices, int64_t n, const double* x, double* out, void* stream) {
+    if (n < 0) return TG_EINVAL;
+    if (n > 0 && (!indices || !x || !out)) return TG_EINVAL;
+    if (n == 0) return TG_OK;
+    const int64_t blocks = std::min<int64_t>(ceil_div(n, 256 * 4), 148 * 16);
+    gather_probe_kernel<I><<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(indices, n, x, out);
+    return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ECUDA;
+}
+
 }  // namespace
 }  // namespace tg
 
@@ -49,10 +61,12 @@ using namespace tg;
 
 extern "C" __attribute__((visibility("default"))) int tg_gather_probe_f64(const int64_t* indices, int64_t n,
                                                                          const double* x, double* out, void* stream) {
-    if (n < 0) return TG_EINVAL;
-    if (n > 0 && (!indices || !x || !out)) return TG_EINVAL;
-    if (n == 0) return TG_OK;
-    const int64_t blocks = std::min<int64_t>(ceil_div(n, 256 * 4), 148 * 16);
-    gather_probe_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(indices, n, x, out);
-    return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ECUDA;
+    return probe_run<int64_t>(indices, n, x, out, stream);
+}
+
+// The same with int32 column indices (a matrix renumbered to 32-bit indices).
+extern "C" __attribute__((visibility("default"))) int tg_gather_probe_i32_f64(const int32_t* indices, int64_t n,
+                                                                             const double* x, double* out,
+                                                                             void* stream) {
+    return probe_run<int32_t>(indices, n, x, out, stream);
 }

@@ -282,6 +282,9 @@ size_t tg_sddmm_workspace_bytes(int64_t rows, int64_t nnz, int64_t k, const tg_s
     rc = check_csr(A, op);                                 \
     if (rc != TG_OK) return rc;                            \
     cudaStream_t st = static_cast<cudaStream_t>(stream);   \
+    if ((sc.flags & TG_FLAG_INDEX32) &&                    \
+        (strncmp(op, "tg_power", 8) != 0 || (sc.flags & TG_FLAG_BOUNDS_CHECK))) \
+        return set_error(TG_EUNSUPPORTED, "%s: 32-bit column indices are taken by the power steps only, without bounds checking", op); \
     if (sc.flags & TG_FLAG_BOUNDS_CHECK) {                 \
         rc = bounds_check(*A, st);                         \
         if (rc != TG_OK) return rc;                        \

@@ -44,6 +44,11 @@ __device__ __forceinline__ int64_t ld_stream(const int64_t* p, uint64_t pol) {
     asm("ld.global.nc.L1::no_allocate.L2::cache_hint.s64 %0, [%1], %2;" : "=l"(v) : "l"(p), "l"(pol));
     return v;
 }
+__device__ __forceinline__ int32_t ld_stream(const int32_t* p, uint64_t pol) {
+    int32_t v;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.s32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol));
+    return v;
+}
 __device__ __forceinline__ double ld_stream(const double* p, uint64_t pol) {
     double v;
     asm("ld.global.nc.L1::no_allocate.L2::cache_hint.f64 %0, [%1], %2;" : "=d"(v) : "l"(p), "l"(pol));
@@ -54,7 +59,12 @@ __device__ __forceinline__ float ld_stream(const float* p, uint64_t pol) {
     asm("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
     return v;
 }
-// 16-byte vector stream loads; the address must be 16-byte aligned.
+// Vector stream loads of two elements; the address must be aligned to their size
+// (16 bytes for 64-bit elements, 8 for 32-bit ones).
+__device__ __forceinline__ void ld_stream2(const int32_t* p, uint64_t pol, int32_t& a, int32_t& b) {
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.s32 {%0, %1}, [%2], %3;"
+        : "=r"(a), "=r"(b) : "l"(p), "l"(pol));
+}
 __device__ __forceinline__ void ld_stream2(const int64_t* p, uint64_t pol, int64_t& a, int64_t& b) {
     asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.s64 {%0, %1}, [%2], %3;"
         : "=l"(a), "=l"(b) : "l"(p), "l"(pol));

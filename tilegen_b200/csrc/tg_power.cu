@@ -21,7 +21,7 @@ namespace tg {
 
 struct PowerArgs {
     const int64_t* indptr;
-    const int64_t* indices;  // renumbered to the padded layout
+    const void* indices;  // renumbered to the padded layout: int64, or int32 (TG_FLAG_INDEX32)
     const double* data;
     const double* x;  // padded input iterate, nparts * stride
     int nparts;
@@ -73,8 +73,9 @@ __device__ __forceinline__ void grid_sum_last(double part, double* partials, uns
     }
 }
 
-template <int TPR, int U, int V>
+template <int TPR, int U, int V, typename I>
 __global__ void __launch_bounds__(512) power_step_kernel(PowerArgs a) {
+    const I* indices = static_cast<const I*>(a.indices);
     __shared__ double s_warp[32];
     __shared__ double s_scale;
     const uint64_t ps = policy_evict_first();
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(512) power_step_kernel(PowerArgs a) {
          base += (int64_t)gridDim.x * a.rows_per_tile) {
         const int64_t end = min(base + a.rows_per_tile, a.rows);
         for (int64_t i = base + group; i < end; i += groups) {
-            double acc = row_dot<double, TPR, U, V>(a.indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
+            double acc = row_dot<double, TPR, U, V, I>(indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
             if constexpr (TPR > 1) acc = group_sum<TPR>(acc, mask);
             if (lane == 0) {
                 const double v = scale * acc;
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(512) power_step_kernel(PowerArgs a) {
 // (tg_power_clear_error) only after every rank agreed to restart from zeroed flags.
 struct PowerP2PArgs {
     const int64_t* indptr;
-    const int64_t* indices;
+    const void* indices;  // int64, or int32 (TG_FLAG_INDEX32)
     const double* data;
     const double* x;  // local padded iterate (nparts * stride)
     int nparts;
@@ -180,8 +181,9 @@ __device__ __forceinline__ bool wait_flags(const unsigned long long* flag_local,
     return true;
 }
 
-template <int TPR, int U, int V>
+template <int TPR, int U, int V, typename I>
 __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
+    const I* indices = static_cast<const I*>(a.indices);
     constexpr int kGroups = 256 / TPR;  // rows per CTA tile: one per lane group
     constexpr int kWarpRows = 32 / TPR; // consecutive rows owned by one warp per tile
     __shared__ double s_warp[32];
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
         const int64_t i = base + group;
         double v = 0.0;
         if (i < rows) {
-            double acc = row_dot<double, TPR, U, V>(a.indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
+            double acc = row_dot<double, TPR, U, V, I>(indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
             if constexpr (TPR > 1) acc = group_sum<TPR>(acc, mask);
             v = scale * acc;
             if (lane == 0) sq = fma(v, v, sq);
@@ -307,38 +309,50 @@ PowerWs carve(void* ws) {
 }
 
 template <int TPR, int U, int V>
-void launch_power(const PowerArgs& a, int blocks, int threads, cudaStream_t st) {
-    power_step_kernel<TPR, U, V><<<blocks, threads, 0, st>>>(a);
+void launch_power(const PowerArgs& a, bool i32, int blocks, int threads, cudaStream_t st) {
+    if (i32)
+        power_step_kernel<TPR, U, V, int32_t><<<blocks, threads, 0, st>>>(a);
+    else
+        power_step_kernel<TPR, U, V, int64_t><<<blocks, threads, 0, st>>>(a);
 }
 
 template <int TPR, int U>
-bool power_v(int v, const PowerArgs& a, int bl, int th, cudaStream_t st) {
+bool power_v(int v, const PowerArgs& a, bool i32, int bl, int th, cudaStream_t st) {
     switch (v) {
-        case 1: launch_power<TPR, U, 1>(a, bl, th, st); return true;
-        case 2: launch_power<TPR, U, 2>(a, bl, th, st); return true;
-        case 4: launch_power<TPR, U, 4>(a, bl, th, st); return true;
+        case 1: launch_power<TPR, U, 1>(a, i32, bl, th, st); return true;
+        case 2: launch_power<TPR, U, 2>(a, i32, bl, th, st); return true;
+        case 4: launch_power<TPR, U, 4>(a, i32, bl, th, st); return true;
     }
     return false;
 }
 
 template <int TPR>
-bool power_u(int u, int v, const PowerArgs& a, int bl, int th, cudaStream_t st) {
+bool power_u(int u, int v, const PowerArgs& a, bool i32, int bl, int th, cudaStream_t st) {
     switch (u) {
-        case 1: return power_v<TPR, 1>(v, a, bl, th, st);
-        case 2: return power_v<TPR, 2>(v, a, bl, th, st);
-        case 4: return power_v<TPR, 4>(v, a, bl, th, st);
+        case 1: return power_v<TPR, 1>(v, a, i32, bl, th, st);
+        case 2: return power_v<TPR, 2>(v, a, i32, bl, th, st);
+        case 4: return power_v<TPR, 4>(v, a, i32, bl, th, st);
     }
     return false;
 }
 
-bool power_dispatch(int tpr, int u, int v, const PowerArgs& a, int bl, int th, cudaStream_t st) {
+bool power_dispatch(int tpr, int u, int v, const PowerArgs& a, bool i32, int bl, int th, cudaStream_t st) {
     switch (tpr) {
-        case 4: return power_u<4>(u, v, a, bl, th, st);
-        case 8: return power_u<8>(u, v, a, bl, th, st);
-        case 16: return power_u<16>(u, v, a, bl, th, st);
-        case 32: return power_u<32>(u, v, a, bl, th, st);
+        case 4: return power_u<4>(u, v, a, i32, bl, th, st);
+        case 8: return power_u<8>(u, v, a, i32, bl, th, st);
+        case 16: return power_u<16>(u, v, a, i32, bl, th, st);
+        case 32: return power_u<32>(u, v, a, i32, bl, th, st);
     }
     return false;
+}
+
+// TG_FLAG_INDEX32: A.indices holds int32 column indices (the padded layout has fewer than
+// 2^31 entries); the vector loads then need 8-byte alignment instead of 16.
+bool index32(const tg_sched& s) { return (s.flags & TG_FLAG_INDEX32) != 0; }
+
+bool stream_aligned(const tg_csr& A, bool i32) {
+    const uintptr_t ia = reinterpret_cast<uintptr_t>(A.indices);
+    return ((i32 ? (ia & 7u) : (ia & 15u)) | (reinterpret_cast<uintptr_t>(A.data) & 15u)) == 0;
 }
 
 }  // namespace
@@ -365,6 +379,9 @@ int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride,
     if (nparts < 1 || stride < A.rows + 1)
         return set_error(TG_EINVAL, "power step: need nparts >= 1 and stride >= rows + 1 (nparts=%d stride=%lld)",
                          nparts, (long long)stride);
+    const bool i32 = index32(s);
+    if (s.split == TG_SPLIT_STREAM && i32)
+        return set_error(TG_EUNSUPPORTED, "power step: 32-bit column indices need the rowwise split");
     if (s.split == TG_SPLIT_STREAM && A.nnz > 0 &&
         ((reinterpret_cast<uintptr_t>(A.indices) | reinterpret_cast<uintptr_t>(A.data) |
           reinterpret_cast<uintptr_t>(A.indptr)) & 15u) == 0)
@@ -382,7 +399,7 @@ int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride,
     const int tpr = s.threads_per_row < 4 ? 4 : s.threads_per_row;
     const int u = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
     int v = s.vector_width;
-    if ((reinterpret_cast<uintptr_t>(A.indices) | reinterpret_cast<uintptr_t>(A.data)) & 15u) v = 1;
+    if (!stream_aligned(A, i32)) v = 1;
     const int threads = s.block_size;
     PowerWs w = carve(ws);
     PowerArgs a{};
@@ -399,14 +416,17 @@ int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride,
     a.ticket = w.ticket;
     int64_t blocks = ceil_div(std::max<int64_t>(A.rows, 1), a.rows_per_tile);
     blocks = std::min<int64_t>(blocks, kPowerMaxGrid);
-    if (!power_dispatch(tpr, u, v, a, (int)blocks, threads, st))
+    if (!power_dispatch(tpr, u, v, a, i32, (int)blocks, threads, st))
         return set_error(TG_EUNSUPPORTED, "no power-step instance for TPR=%d U=%d V=%d", tpr, u, v);
     return check_launch("power_step_kernel");
 }
 
 template <int TPR, int U, int V>
-static void launch_p2p(const PowerP2PArgs& a, int blocks, cudaStream_t st) {
-    power_p2p_kernel<TPR, U, V><<<blocks, 256, 0, st>>>(a);
+static void launch_p2p(const PowerP2PArgs& a, bool i32, int blocks, cudaStream_t st) {
+    if (i32)
+        power_p2p_kernel<TPR, U, V, int32_t><<<blocks, 256, 0, st>>>(a);
+    else
+        power_p2p_kernel<TPR, U, V, int64_t><<<blocks, 256, 0, st>>>(a);
 }
 
 int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, int64_t stride,
@@ -439,16 +459,16 @@ int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, i
     a.err = p2p_err_word(ws);
     const int tpr = s.threads_per_row <= 4 ? 4 : 8;
     const int u = s.unroll >= 2 ? 2 : 1;
+    const bool i32 = index32(s);
     int v = s.vector_width >= 2 ? 2 : 1;
-    if ((reinterpret_cast<uintptr_t>(A.indices) | reinterpret_cast<uintptr_t>(A.data)) & 15u) v = 1;
-    int64_t blocks = ceil_div(std::max<int64_t>(A.rows, 1), 256 / tpr);
-    blocks = std::min<int64_t>(blocks, kPowerMaxGrid);
+    if (!stream_aligned(A, i32)) v = 1;
+    const int bl = (int)std::min<int64_t>(ceil_div(std::max<int64_t>(A.rows, 1), 256 / tpr), kPowerMaxGrid);
     if (tpr == 4) {
-        if (u == 2) { if (v == 2) launch_p2p<4, 2, 2>(a, (int)blocks, st); else launch_p2p<4, 2, 1>(a, (int)blocks, st); }
-        else { if (v == 2) launch_p2p<4, 1, 2>(a, (int)blocks, st); else launch_p2p<4, 1, 1>(a, (int)blocks, st); }
+        if (u == 2) { if (v == 2) launch_p2p<4, 2, 2>(a, i32, bl, st); else launch_p2p<4, 2, 1>(a, i32, bl, st); }
+        else { if (v == 2) launch_p2p<4, 1, 2>(a, i32, bl, st); else launch_p2p<4, 1, 1>(a, i32, bl, st); }
     } else {
-        if (u == 2) { if (v == 2) launch_p2p<8, 2, 2>(a, (int)blocks, st); else launch_p2p<8, 2, 1>(a, (int)blocks, st); }
-        else { if (v == 2) launch_p2p<8, 1, 2>(a, (int)blocks, st); else launch_p2p<8, 1, 1>(a, (int)blocks, st); }
+        if (u == 2) { if (v == 2) launch_p2p<8, 2, 2>(a, i32, bl, st); else launch_p2p<8, 2, 1>(a, i32, bl, st); }
+        else { if (v == 2) launch_p2p<8, 1, 2>(a, i32, bl, st); else launch_p2p<8, 1, 1>(a, i32, bl, st); }
     }
     return check_launch("power_p2p_kernel");
 }

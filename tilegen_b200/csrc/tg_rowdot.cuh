@@ -9,23 +9,31 @@
 
 namespace tg {
 
-template <typename T, int V>
-__device__ __forceinline__ void ld_stream_vec(const int64_t* pi, const T* pv, uint64_t pol, int64_t (&c)[V],
-                                              T (&v)[V]) {
+// V column indices (int64, or int32 where a caller stored them narrower) and V values
+// starting at a V-element boundary.
+template <typename T, typename I, int V>
+__device__ __forceinline__ void ld_stream_vec(const I* pi, const T* pv, uint64_t pol, int64_t (&c)[V], T (&v)[V]) {
     if constexpr (V == 1) {
         c[0] = ld_stream(pi, pol);
         v[0] = ld_stream(pv, pol);
     } else {
 #pragma unroll
-        for (int e = 0; e < V; e += 2) ld_stream2(pi + e, pol, c[e], c[e + 1]);
+        for (int e = 0; e < V; e += 2) {
+            I a, b;
+            ld_stream2(pi + e, pol, a, b);
+            c[e] = a;
+            c[e + 1] = b;
+        }
 #pragma unroll
         for (int e = 0; e < V; e += 2) ld_stream2(pv + e, pol, v[e], v[e + 1]);
     }
 }
 
 // Dot product of row [p, pe) with x by the TPR lanes of one group (this lane's share).
-template <typename T, int TPR, int U, int V>
-__device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* __restrict__ val,
+// I is the column index type (int64_t, or int32_t for a matrix the caller renumbered to
+// 32-bit indices).
+template <typename T, int TPR, int U, int V, typename I = int64_t>
+__device__ __forceinline__ T row_dot(const I* __restrict__ idx, const T* __restrict__ val,
                                      const T* __restrict__ x, int64_t p, int64_t pe, int lane, uint64_t ps,
                                      uint64_t pg) {
     Sum<T> acc;
@@ -36,7 +44,7 @@ __device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* _
             T v[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                c[u] = ld_stream(idx + q + u * TPR, ps);
+                c[u] = (int64_t)ld_stream(idx + q + u * TPR, ps);
                 v[u] = ld_stream(val + q + u * TPR, ps);
             }
 #pragma unroll
@@ -57,7 +65,7 @@ __device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* _
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int64_t q = pa + (k + (int64_t)u * TPR) * V;
-                ld_stream_vec<T, V>(idx + q, val + q, ps, c[u], v[u]);
+                ld_stream_vec<T, I, V>(idx + q, val + q, ps, c[u], v[u]);
             }
 #pragma unroll
             for (int u = 0; u < U; ++u)
@@ -68,7 +76,7 @@ __device__ __forceinline__ T row_dot(const int64_t* __restrict__ idx, const T* _
             int64_t c[V];
             T v[V];
             const int64_t q = pa + k * V;
-            ld_stream_vec<T, V>(idx + q, val + q, ps, c, v);
+            ld_stream_vec<T, I, V>(idx + q, val + q, ps, c, v);
 #pragma unroll
             for (int e = 0; e < V; ++e) acc.mad(v[e], ld_gather(x + c[e], pg));
         }

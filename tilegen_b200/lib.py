@@ -33,6 +33,7 @@ TG_SPLIT_BLOCK = 4
 TG_FLAG_BOUNDS_CHECK = 1
 TG_FLAG_INJECT_BUG = 2
 TG_FLAG_REUSE_PLAN = 4
+TG_FLAG_INDEX32 = 8
 
 STATUS_NAMES = {
     TG_OK: "TG_OK",
@@ -107,6 +108,8 @@ SIGNATURES = {
                                          ctypes.c_void_p, _SP, ctypes.c_double]),
     "tg_renumber_columns": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                            ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p]),
+    "tg_renumber_columns_i32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                               ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p]),
     "tg_default_schedule": (None, [_SP]),
     "tg_validate_schedule": (ctypes.c_int, [_SP]),
     "tg_set_schedule": (ctypes.c_int, [_SP]),

@@ -51,10 +51,11 @@ def padded_stride(bounds: np.ndarray, align: int = 32) -> int:
     return ((longest + 1 + align - 1) // align) * align
 
 
-def renumber_columns(indices, bounds, stride: int):
+def renumber_columns(indices, bounds, stride: int, index32: bool = False):
     """j -> owner(j) * stride + (j - bounds[owner(j)]).  CUDA tensors go through the
-    library's kernel (tg_renumber_columns, on the current stream); numpy arrays and CPU
-    tensors are renumbered on the host (the gloo tests)."""
+    library's kernel (tg_renumber_columns, or tg_renumber_columns_i32 with ``index32``:
+    int32 output, which the power steps read with TG_FLAG_INDEX32), on the current
+    stream; numpy arrays and CPU tensors are renumbered on the host (the gloo tests)."""
     try:
         import torch
 
@@ -64,12 +65,13 @@ def renumber_columns(indices, bounds, stride: int):
 
                 L = _lib.load()
                 idx = indices.contiguous().to(torch.int64)
-                out = torch.empty_like(idx)
+                out = torch.empty(idx.numel(), dtype=torch.int32 if index32 else torch.int64, device=idx.device)
+                fn = L.tg_renumber_columns_i32 if index32 else L.tg_renumber_columns
                 b = np.ascontiguousarray(bounds, dtype=np.int64)
                 with torch.cuda.device(idx.device):
                     st = torch.cuda.current_stream(idx.device).cuda_stream
-                    _lib.check(L.tg_renumber_columns(idx.data_ptr(), out.data_ptr(), idx.numel(), b.ctypes.data,
-                                                     b.size - 1, int(stride), st), "tg_renumber_columns")
+                    _lib.check(fn(idx.data_ptr(), out.data_ptr(), idx.numel(), b.ctypes.data, b.size - 1, int(stride),
+                                  st), "tg_renumber_columns")
                 return out
             return torch.from_numpy(renumber_columns(indices.numpy(), bounds, stride))
     except ImportError:  # pragma: no cover
@@ -130,12 +132,17 @@ class PowerIteration:
     ``finalize`` (``finalize(x_full, x_out, lam_out)``) and ``exchange``
     (``exchange(x_full)``, all-gathers the shards in place).  The custom hooks exist for
     host-side tests of the sharding logic; the defaults are the GPU kernels.
+
+    ``index32`` (default: whenever the GPU steps run the rowwise split and the padded
+    layout has fewer than 2^31 entries) keeps the renumbered column indices as int32, so
+    every step streams 12 bytes per nonzero instead of 16; the matrix is renumbered once,
+    here, and read by every step.
     """
 
     def __init__(self, indptr, indices, data, bounds: Sequence[int], rank: int, sched=None,
                  step: Optional[Callable] = None, norm2: Optional[Callable] = None,
                  finalize: Optional[Callable] = None, exchange: Optional[Callable] = None,
-                 renumber: bool = True):
+                 renumber: bool = True, index32: Optional[bool] = None):
         import torch
 
         self.torch = torch
@@ -149,7 +156,14 @@ class PowerIteration:
         if int(indptr.numel()) != self.rows + 1:
             raise ValueError("indptr has %d entries for a %d-row shard" % (indptr.numel(), self.rows))
         self.indptr = indptr
-        self.indices = renumber_columns(indices, self.bounds, self.stride) if renumber else indices
+        gpu = step is None and norm2 is None and finalize is None and getattr(indices, "is_cuda", False)
+        if index32 is None:
+            split = getattr(sched, "split", 0) if sched is not None else 0
+            index32 = gpu and renumber and split == 0 and self.parts * self.stride < 2 ** 31
+        if index32 and not (gpu and renumber):
+            raise ValueError("index32 needs the GPU steps and renumber=True")
+        self.index32 = bool(index32)
+        self.indices = (renumber_columns(indices, self.bounds, self.stride, self.index32) if renumber else indices)
         self.data = data
         self.nnz = int(indices.numel())
         n = self.parts * self.stride
@@ -169,6 +183,9 @@ class PowerIteration:
             self._lib = _lib
             L = _lib.load()
             self._sched_c = sched if sched is not None else self._default_sched()
+            if self.index32:
+                self._sched_c = self._lib.TgSched(*[getattr(self._sched_c, f) for f, _ in self._sched_c._fields_])
+                self._sched_c.flags |= self._lib.TG_FLAG_INDEX32
             self.ws = torch.zeros(int(L.tg_power_workspace_bytes(self.nnz, ctypes.byref(self._sched_c))),
                                   dtype=torch.uint8, device=self.device)
             self._desc = _lib.TgCsr(self.rows, n, self.nnz, self.indptr.data_ptr(), self.indices.data_ptr(),
