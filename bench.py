@@ -83,6 +83,9 @@ def parse():
     ap.add_argument("--block", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
+    ap.add_argument("--index-bits", type=int, choices=[32, 64], default=32,
+                    help="c4: width of the renumbered column indices the power steps stream (32: 12 bytes "
+                         "per nonzero, 64: 16)")
     ap.add_argument("--no-workloads", action="store_true",
                     help="c4: skip the C1-C3 / C5 measurements that the default line carries in `workloads`")
     args = ap.parse_args()
@@ -872,7 +875,8 @@ def main():
     d_ix = h_ix.to(dev)
     d_d = h_d.to(dev)
     d_x0 = h_x0.to(dev)
-    pi = PowerIteration(d_ip, d_ix, d_d, bounds, rank, sched=s)
+    i32 = args.index_bits == 32 and args.split != "stream"
+    pi = PowerIteration(d_ip, d_ix, d_d, bounds, rank, sched=s, index32=i32)
     if world > 1 and args.exchange == "p2p":
         pi.p2p_connect()
     del d_ix
@@ -965,7 +969,7 @@ def main():
         ix = h_ix.to(dev, non_blocking=True)
         dd = h_d.to(dev, non_blocking=True)
         xx = h_x0.to(dev, non_blocking=True)
-        pe = PowerIteration(ip, ix, dd, bounds, rank, sched=s)
+        pe = PowerIteration(ip, ix, dd, bounds, rank, sched=s, index32=i32)
         if world > 1 and args.exchange == "p2p":
             pe.p2p_attach(pi.exchange_state)  # the mappings do not depend on the matrix
         del ix
@@ -1061,7 +1065,7 @@ def main():
             "clocks": clocks,
             "wall_s_timed": round(wall, 4),
             "schedule": {"split": args.split, "tpr": args.tpr, "unroll": args.unroll, "vec": args.vec,
-                         "block": args.block},
+                         "block": args.block, "column_index_bits": 32 if pi.index32 else 64},
             "lambda": float(lam[0].item()),  # the timed steps' result (rank 0's copy)
         }
         if world > 1:
@@ -1095,7 +1099,12 @@ def cusparse_c4(pi, n: int, dev, nbytes: int, reps: int = 10):
     import torch
 
     try:
-        Sp = torch.sparse_csr_tensor(pi.indptr, pi.indices, pi.data, size=(n, n))
+        # cuSPARSE needs row offsets and column indices of one type: the power iteration
+        # keeps its columns as int32, so the comparison gets an int64 copy
+        cols = pi.indices if pi.indices.dtype == pi.indptr.dtype else pi.indices.to(pi.indptr.dtype)
+        if cols.dtype != pi.indptr.dtype or cols.numel() != pi.nnz:
+            raise ValueError("index arrays of the comparison do not match")
+        Sp = torch.sparse_csr_tensor(pi.indptr, cols, pi.data, size=(n, n))
         x = pi.x[0][:n].clone()
         for _ in range(3):
             torch.mv(Sp, x)

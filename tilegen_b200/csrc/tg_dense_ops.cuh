@@ -335,38 +335,44 @@ __global__ void __launch_bounds__(256) group_plan_kernel(const int64_t* __restri
     }
 }
 
-// One warp per group, grid-stride.  Lane l owns the VEC columns s + l*VEC of each 32*VEC
-// column slice s of this launch's tile.  Positions are read 32 at a time (one coalesced
-// load of indices and of each row's values per 32 positions) and handed out by shuffles;
-// UG gathers are in flight per lane.
+// One warp per (group, column slice) task, grid-stride; the slices of a group go to
+// neighbouring warps, which share the group's index and value loads through L1.  Lane l
+// owns the VEC columns s + l*VEC of slice s (32*VEC columns).  Positions are read 32 at a
+// time (one coalesced load of indices and of each row's values per 32 positions) and
+// handed out by shuffles; UG gathers are in flight per lane.
 template <typename T, int VEC, int UG>
-__global__ void __launch_bounds__(256) spmm_group_kernel(DenseArgs<T> a, const uint8_t* __restrict__ flag,
+__global__ void __launch_bounds__(256, 3) spmm_group_kernel(DenseArgs<T> a, const uint8_t* __restrict__ flag,
                                                          int64_t ngroups) {
     constexpr int R = kGroupRows;
     const int lane = threadIdx.x % kWarp;
     const int64_t nw = ((int64_t)gridDim.x * blockDim.x) / kWarp;
     const uint64_t ps = policy_evict_first();
     const uint64_t pg = policy_evict_last();
-    for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / kWarp; g < ngroups; g += nw) {
+    const int64_t nslices = (a.kt + (int64_t)kWarp * VEC - 1) / ((int64_t)kWarp * VEC);
+    for (int64_t task = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / kWarp; task < ngroups * nslices;
+         task += nw) {
+        const int64_t g = task / nslices;
         const int64_t r0 = g * R;
         const bool grouped = flag[g] != 0;
         const int nrows = (int)min((int64_t)R, a.rows - r0);
-        for (int64_t s0 = 0; s0 < a.kt; s0 += (int64_t)kWarp * VEC) {
+        {
+            const int64_t s0 = (task % nslices) * (int64_t)kWarp * VEC;
             const int64_t col = s0 + (int64_t)lane * VEC;
             const bool live = col < a.kt;
             if (grouped) {
-                int64_t base[R];
-#pragma unroll
-                for (int r = 0; r < R; ++r) base[r] = a.indptr[r0 + r];
-                const int64_t len = a.indptr[r0 + 1] - base[0];
+                // the rows of a flagged group have one column list, hence one length:
+                // row r starts at base + r * len
+                const int64_t base = a.indptr[r0];
+                const int64_t len = a.indptr[r0 + 1] - base;
                 Sum<T> acc[R][VEC];
                 for (int64_t p0 = 0; p0 < len; p0 += kWarp) {
                     const int n = (int)min((int64_t)kWarp, len - p0);
                     int64_t myidx = 0;
                     T myval[R];
-                    if (lane < n) myidx = ld_stream(a.indices + base[0] + p0 + lane, ps);
+                    if (lane < n) myidx = ld_stream(a.indices + base + p0 + lane, ps);
 #pragma unroll
-                    for (int r = 0; r < R; ++r) myval[r] = lane < n ? ld_stream(a.data + base[r] + p0 + lane, ps) : T(0);
+                    for (int r = 0; r < R; ++r)
+                        myval[r] = lane < n ? ld_stream(a.data + base + r * len + p0 + lane, ps) : T(0);
                     for (int j0 = 0; j0 < n; j0 += UG) {
                         Vec<T, VEC> b[UG];
 #pragma unroll
