@@ -83,7 +83,7 @@ def parse():
     ap.add_argument("--block", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
-    ap.add_argument("--index-bits", type=int, choices=[32, 64], default=32,
+    ap.add_argument("--index-bits", type=int, choices=[32, 64], default=64,
                     help="c4: width of the renumbered column indices the power steps stream (32: 12 bytes "
                          "per nonzero, 64: 16)")
     ap.add_argument("--no-workloads", action="store_true",
@@ -683,6 +683,8 @@ def summarise_matrix(rec, ms_step: float, world: int, peak: float):
          "roofline_frac": round(achieved / peak, 4), "algorithmic_bytes": int(total),
          "l2": "flushed before every call" if rec["flush"] else "inputs larger than L2",
          "schedule": rec["schedule"], "gpu_launches": rec["launches"]}
+    tr = traffic_record("%s_%d" % (wl, world), matrix_kernel_name(rec["kernel"], rec["schedule"]["split"]))
+    d["traffic_bytes"] = tr["dram_bytes_per_launch"] if tr else None
     if rec.get("plan"):
         d["plan"] = rec["plan"]
     if rec.get("floor"):

@@ -59,6 +59,12 @@ __device__ __forceinline__ float ld_stream(const float* p, uint64_t pol) {
     asm("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
     return v;
 }
+// Four int32 stream elements in one 16-byte load; the address must be 16-byte aligned.
+__device__ __forceinline__ void ld_stream4(const int32_t* p, uint64_t pol, int32_t& a, int32_t& b, int32_t& c,
+                                           int32_t& d) {
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.s32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "l"(p), "l"(pol));
+}
 // Vector stream loads of two elements; the address must be aligned to their size
 // (16 bytes for 64-bit elements, 8 for 32-bit ones).
 __device__ __forceinline__ void ld_stream2(const int32_t* p, uint64_t pol, int32_t& a, int32_t& b) {

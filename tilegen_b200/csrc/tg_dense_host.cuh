@@ -187,17 +187,18 @@ int spmm_groups_run(const tg_csr& A, const T* B, T* C, int64_t K, const tg_sched
     uint8_t* flag = static_cast<uint8_t*>(ws);
     const int64_t warps_per_cta = 256 / kWarp;
     const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(ngroups, warps_per_cta), 148 * 32));
-    const int64_t tasks = ngroups * ceil_div(K, 2 * kWarp);
-    const int64_t blocks_run = std::max<int64_t>(1, std::min<int64_t>(ceil_div(tasks, warps_per_cta), 148 * 32));
     if (!(s.flags & TG_FLAG_REUSE_PLAN)) {
         group_plan_kernel<kGroupRows><<<(unsigned)blocks, 256, 0, st>>>(A.indptr, A.indices, A.rows, ngroups, flag);
         const int rc = check_launch("group_plan_kernel");
         if (rc != TG_OK) return rc;
     }
-    // two elements per lane (64 fp32 / 64 fp64 columns per warp task): eight rows of
-    // accumulators stay within a register budget that keeps 3 CTAs of 256 threads per SM
-    int vec = 2;
+    // one 16-byte vector per lane (128 fp32 / 64 fp64 columns per warp task): splitting a
+    // group's columns over more warps repeats its index and value loads and shuffles per
+    // warp, which measured slower on the blocked class (73.2 vs 67.6 us)
+    int vec = sizeof(T) == 4 ? 4 : 2;
     while (vec > 1 && (K % vec != 0 || !aligned_to(B, vec * sizeof(T)) || !aligned_to(C, vec * sizeof(T)))) vec /= 2;
+    const int64_t tasks = ngroups * ceil_div(K, (int64_t)vec * kWarp);
+    const int64_t blocks_run = std::max<int64_t>(1, std::min<int64_t>(ceil_div(tasks, warps_per_cta), 148 * 32));
     DenseArgs<T> a{};
     a.indptr = A.indptr;
     a.indices = A.indices;
@@ -209,10 +210,13 @@ int spmm_groups_run(const tg_csr& A, const T* B, T* C, int64_t K, const tg_sched
     a.B = B;
     a.C = C;
     a.kt = K;
-    if (vec == 2)
+    if (vec == 4) {
+        if constexpr (sizeof(T) == 4) spmm_group_kernel<T, 4, 4><<<(unsigned)blocks_run, 256, 0, st>>>(a, flag, ngroups);
+    } else if (vec == 2) {
         spmm_group_kernel<T, 2, 4><<<(unsigned)blocks_run, 256, 0, st>>>(a, flag, ngroups);
-    else
+    } else {
         spmm_group_kernel<T, 1, 4><<<(unsigned)blocks_run, 256, 0, st>>>(a, flag, ngroups);
+    }
     return check_launch("spmm_group_kernel");
 }
 

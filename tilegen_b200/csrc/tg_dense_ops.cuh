@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(256) group_plan_kernel(const int64_t* __restri
 // time (one coalesced load of indices and of each row's values per 32 positions) and
 // handed out by shuffles; UG gathers are in flight per lane.
 template <typename T, int VEC, int UG>
-__global__ void __launch_bounds__(256, 3) spmm_group_kernel(DenseArgs<T> a, const uint8_t* __restrict__ flag,
+__global__ void __launch_bounds__(256) spmm_group_kernel(DenseArgs<T> a, const uint8_t* __restrict__ flag,
                                                          int64_t ngroups) {
     constexpr int R = kGroupRows;
     const int lane = threadIdx.x % kWarp;

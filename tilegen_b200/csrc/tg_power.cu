@@ -347,12 +347,13 @@ bool power_dispatch(int tpr, int u, int v, const PowerArgs& a, bool i32, int bl,
 }
 
 // TG_FLAG_INDEX32: A.indices holds int32 column indices (the padded layout has fewer than
-// 2^31 entries); the vector loads then need 8-byte alignment instead of 16.
+// 2^31 entries); pairs of them need 8-byte alignment, quads (V = 4) 16.
 bool index32(const tg_sched& s) { return (s.flags & TG_FLAG_INDEX32) != 0; }
 
-bool stream_aligned(const tg_csr& A, bool i32) {
+bool stream_aligned(const tg_csr& A, bool i32, int v) {
     const uintptr_t ia = reinterpret_cast<uintptr_t>(A.indices);
-    return ((i32 ? (ia & 7u) : (ia & 15u)) | (reinterpret_cast<uintptr_t>(A.data) & 15u)) == 0;
+    const uintptr_t need = (i32 && v < 4) ? 7u : 15u;
+    return ((ia & need) | (reinterpret_cast<uintptr_t>(A.data) & 15u)) == 0;
 }
 
 }  // namespace
@@ -399,7 +400,7 @@ int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride,
     const int tpr = s.threads_per_row < 4 ? 4 : s.threads_per_row;
     const int u = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
     int v = s.vector_width;
-    if (!stream_aligned(A, i32)) v = 1;
+    while (v > 1 && !stream_aligned(A, i32, v)) v /= 2;
     const int threads = s.block_size;
     PowerWs w = carve(ws);
     PowerArgs a{};
@@ -461,7 +462,7 @@ int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, i
     const int u = s.unroll >= 2 ? 2 : 1;
     const bool i32 = index32(s);
     int v = s.vector_width >= 2 ? 2 : 1;
-    if (!stream_aligned(A, i32)) v = 1;
+    if (!stream_aligned(A, i32, v)) v = 1;
     const int bl = (int)std::min<int64_t>(ceil_div(std::max<int64_t>(A.rows, 1), 256 / tpr), kPowerMaxGrid);
     if (tpr == 4) {
         if (u == 2) { if (v == 2) launch_p2p<4, 2, 2>(a, i32, bl, st); else launch_p2p<4, 2, 1>(a, i32, bl, st); }

@@ -17,12 +17,21 @@ __device__ __forceinline__ void ld_stream_vec(const I* pi, const T* pv, uint64_t
         c[0] = ld_stream(pi, pol);
         v[0] = ld_stream(pv, pol);
     } else {
+        if constexpr (sizeof(I) == 4 && V == 4) {  // four 32-bit indices in one 16-byte load
+            int32_t a, b, d, e;
+            ld_stream4(pi, pol, a, b, d, e);
+            c[0] = a;
+            c[1] = b;
+            c[2] = d;
+            c[3] = e;
+        } else {
 #pragma unroll
-        for (int e = 0; e < V; e += 2) {
-            I a, b;
-            ld_stream2(pi + e, pol, a, b);
-            c[e] = a;
-            c[e + 1] = b;
+            for (int e = 0; e < V; e += 2) {
+                I a, b;
+                ld_stream2(pi + e, pol, a, b);
+                c[e] = a;
+                c[e + 1] = b;
+            }
         }
 #pragma unroll
         for (int e = 0; e < V; e += 2) ld_stream2(pv + e, pol, v[e], v[e + 1]);

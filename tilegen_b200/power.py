@@ -133,16 +133,17 @@ class PowerIteration:
     (``exchange(x_full)``, all-gathers the shards in place).  The custom hooks exist for
     host-side tests of the sharding logic; the defaults are the GPU kernels.
 
-    ``index32`` (default: whenever the GPU steps run the rowwise split and the padded
-    layout has fewer than 2^31 entries) keeps the renumbered column indices as int32, so
-    every step streams 12 bytes per nonzero instead of 16; the matrix is renumbered once,
-    here, and read by every step.
+    ``index32`` keeps the renumbered column indices as int32 (the GPU steps, rowwise
+    split, padded layout below 2^31 entries), so every step streams 12 bytes per nonzero
+    instead of 16; the matrix is renumbered once, here, and read by every step.  Off by
+    default: on the 8M-row C4 matrix it measured slower than int64 indices (1.285 vs 1.249
+    ms per step), although it is faster on a 2M-row one.
     """
 
     def __init__(self, indptr, indices, data, bounds: Sequence[int], rank: int, sched=None,
                  step: Optional[Callable] = None, norm2: Optional[Callable] = None,
                  finalize: Optional[Callable] = None, exchange: Optional[Callable] = None,
-                 renumber: bool = True, index32: Optional[bool] = None):
+                 renumber: bool = True, index32: bool = False):
         import torch
 
         self.torch = torch
@@ -157,11 +158,8 @@ class PowerIteration:
             raise ValueError("indptr has %d entries for a %d-row shard" % (indptr.numel(), self.rows))
         self.indptr = indptr
         gpu = step is None and norm2 is None and finalize is None and getattr(indices, "is_cuda", False)
-        if index32 is None:
-            split = getattr(sched, "split", 0) if sched is not None else 0
-            index32 = gpu and renumber and split == 0 and self.parts * self.stride < 2 ** 31
-        if index32 and not (gpu and renumber):
-            raise ValueError("index32 needs the GPU steps and renumber=True")
+        if index32 and not (gpu and renumber and self.parts * self.stride < 2 ** 31):
+            raise ValueError("index32 needs the GPU steps, renumber=True and a padded layout below 2^31")
         self.index32 = bool(index32)
         self.indices = (renumber_columns(indices, self.bounds, self.stride, self.index32) if renumber else indices)
         self.data = data
