@@ -51,7 +51,7 @@ FALLBACK_HBM_GBS = 6650.0
 WORKLOADS = ("c4", "c1", "c2", "c3", "c5-spmm", "c5-sddmm", "c5-spmm-rcm", "blocked-spmm")
 # Default schedule per workload: the fastest measured in the schedule sweeps on a B200.
 SCHEDULES = {
-    "c4": {"split": "rowwise", "tpr": 4, "unroll": 2, "vec": 2, "block": 256},
+    "c4": {"split": "rowwise", "tpr": 4, "unroll": 1, "vec": 4, "block": 256},
     "c1": {"split": "rowwise", "tpr": 4, "unroll": 2, "vec": 2, "block": 128},
     "c2": {"split": "merge", "tpr": 8, "unroll": 2, "vec": 2, "block": 256},
     "c3": {"split": "merge", "tpr": 8, "unroll": 2, "vec": 2, "block": 256},
@@ -83,7 +83,7 @@ def parse():
     ap.add_argument("--block", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
-    ap.add_argument("--index-bits", type=int, choices=[32, 64], default=64,
+    ap.add_argument("--index-bits", type=int, choices=[32, 64], default=32,
                     help="c4: width of the renumbered column indices the power steps stream (32: 12 bytes "
                          "per nonzero, 64: 16)")
     ap.add_argument("--no-workloads", action="store_true",

@@ -41,10 +41,11 @@ def _worker(rank, world, port, mode, q):
         a, b = int(bounds[rank]), int(bounds[rank + 1])
         sh = M.c4_rows(a, b, n=N_ROWS, per_row=32, seed=4)
         s = lib.default_schedule()
-        s.threads_per_row, s.unroll, s.vector_width, s.block_size = 4, 2, 2, 256
+        s.threads_per_row, s.unroll, s.vector_width, s.block_size = (4, 1, 4, 256) if mode == "p2p-v4" else (4, 2, 2, 256)
         pi = PowerIteration(torch.as_tensor(sh.indptr).to(dev), torch.as_tensor(sh.indices).to(dev),
                             torch.as_tensor(sh.data).to(dev), bounds, rank, sched=s)
-        if mode == "p2p":
+        assert pi.index32 == (mode == "p2p-v4")
+        if mode.startswith("p2p"):
             pi.p2p_connect()
         x0 = np.random.default_rng(3).uniform(-1, 1, N_ROWS)
         res = []
@@ -54,8 +55,8 @@ def _worker(rank, world, port, mode, q):
             x, lam = pi.result()
             torch.cuda.synchronize()
             res.append((x.cpu().numpy(), float(lam[0])))
-        err = pi.error_word() if mode == "p2p" else 0
-        if mode == "p2p":
+        err = pi.error_word() if mode.startswith("p2p") else 0
+        if mode.startswith("p2p"):
             pi.close()
         q.put((rank, res, err))
         dist.barrier()
@@ -63,7 +64,7 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["nccl", "p2p"])
+@pytest.mark.parametrize("mode", ["nccl", "p2p", "p2p-v4"])
 def test_power_iteration_two_gpus(mode):
     world = min(torch.cuda.device_count(), 2)
     if world < 2:

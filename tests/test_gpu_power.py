@@ -28,7 +28,8 @@ def rel(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-300))
 
 
-@pytest.mark.parametrize("tpr,u,v,split", [(4, 1, 1, "rowwise"), (8, 2, 2, "rowwise"), (16, 4, 2, "rowwise"),
+@pytest.mark.parametrize("tpr,u,v,split", [(4, 1, 1, "rowwise"), (4, 1, 4, "rowwise"), (8, 2, 2, "rowwise"),
+                                           (16, 4, 2, "rowwise"),
                                            (32, 2, 4, "rowwise"), (4, 1, 1, "stream"), (4, 2, 2, "stream"),
                                            (4, 4, 2, "stream"), (4, 8, 2, "stream")])
 def test_power_iteration_single_gpu_matches_oracle(tpr, u, v, split):
@@ -106,8 +107,9 @@ def test_power_step_is_deterministic(split):
     assert np.array_equal(outs[0], outs[1])
 
 
+@pytest.mark.parametrize("vec", [2, 4])
 @pytest.mark.parametrize("parts", [2, 3, 8])
-def test_p2p_fused_step_emulated_on_one_gpu(parts):
+def test_p2p_fused_step_emulated_on_one_gpu(parts, vec):
     """tg_power_step_p2p_f64 with every rank's buffers on one device: per epoch the
     ranks' kernels run one after another on one stream, so each wait is already met when
     its kernel starts (nothing waits on a kernel that has not run).  Checks the pushes
@@ -122,8 +124,9 @@ def test_p2p_fused_step_emulated_on_one_gpu(parts):
         ip = A.indptr[a:b + 1] - A.indptr[a]
         sl = slice(int(A.indptr[a]), int(A.indptr[b]))
         pis.append(PowerIteration(torch.as_tensor(ip).to(dev), torch.as_tensor(A.indices[sl]).to(dev),
-                                  torch.as_tensor(A.data[sl]).to(dev), bounds, r, sched=_sched(4, 2, 2),
-                                  exchange=lambda x: None))
+                                  torch.as_tensor(A.data[sl]).to(dev), bounds, r,
+                                  sched=_sched(4, 2, 2) if vec == 2 else _sched(4, 1, 4), exchange=lambda x: None))
+    assert all(p.index32 == (vec == 4) for p in pis)  # int32 indices by default with V=4
     flags = [torch.zeros(parts, dtype=torch.int64, device=dev) for _ in range(parts)]
     for pi in pis:
         pi.p2p_setup([(q.x[0], q.x[1]) for q in pis], flags)

@@ -461,15 +461,22 @@ int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, i
     const int tpr = s.threads_per_row <= 4 ? 4 : 8;
     const int u = s.unroll >= 2 ? 2 : 1;
     const bool i32 = index32(s);
-    int v = s.vector_width >= 2 ? 2 : 1;
-    if (!stream_aligned(A, i32, v)) v = 1;
+    int v = s.vector_width >= 4 ? 4 : (s.vector_width >= 2 ? 2 : 1);
+    while (v > 1 && !stream_aligned(A, i32, v)) v /= 2;
     const int bl = (int)std::min<int64_t>(ceil_div(std::max<int64_t>(A.rows, 1), 256 / tpr), kPowerMaxGrid);
     if (tpr == 4) {
-        if (u == 2) { if (v == 2) launch_p2p<4, 2, 2>(a, i32, bl, st); else launch_p2p<4, 2, 1>(a, i32, bl, st); }
-        else { if (v == 2) launch_p2p<4, 1, 2>(a, i32, bl, st); else launch_p2p<4, 1, 1>(a, i32, bl, st); }
+        if (u == 2) {
+            if (v == 4) launch_p2p<4, 2, 4>(a, i32, bl, st);
+            else if (v == 2) launch_p2p<4, 2, 2>(a, i32, bl, st);
+            else launch_p2p<4, 2, 1>(a, i32, bl, st);
+        } else {
+            if (v == 4) launch_p2p<4, 1, 4>(a, i32, bl, st);
+            else if (v == 2) launch_p2p<4, 1, 2>(a, i32, bl, st);
+            else launch_p2p<4, 1, 1>(a, i32, bl, st);
+        }
     } else {
-        if (u == 2) { if (v == 2) launch_p2p<8, 2, 2>(a, i32, bl, st); else launch_p2p<8, 2, 1>(a, i32, bl, st); }
-        else { if (v == 2) launch_p2p<8, 1, 2>(a, i32, bl, st); else launch_p2p<8, 1, 1>(a, i32, bl, st); }
+        if (u == 2) { if (v >= 2) launch_p2p<8, 2, 2>(a, i32, bl, st); else launch_p2p<8, 2, 1>(a, i32, bl, st); }
+        else { if (v >= 2) launch_p2p<8, 1, 2>(a, i32, bl, st); else launch_p2p<8, 1, 1>(a, i32, bl, st); }
     }
     return check_launch("power_p2p_kernel");
 }

@@ -135,15 +135,17 @@ class PowerIteration:
 
     ``index32`` keeps the renumbered column indices as int32 (the GPU steps, rowwise
     split, padded layout below 2^31 entries), so every step streams 12 bytes per nonzero
-    instead of 16; the matrix is renumbered once, here, and read by every step.  Off by
-    default: on the 8M-row C4 matrix it measured slower than int64 indices (1.285 vs 1.249
-    ms per step), although it is faster on a 2M-row one.
+    instead of 16; the matrix is renumbered once, here, and read by every step.  The
+    default (None) turns it on with 16-byte index loads (vector_width 4), the schedule
+    where it measured faster on the 8M-row C4 matrix (1.193 ms per step at TPR4 U1 V4,
+    against 1.234 ms for the best int64 schedule, TPR4 U2 V2); with pairs of indices
+    (vector_width 2) it measured slower (1.301 ms) and stays off.
     """
 
     def __init__(self, indptr, indices, data, bounds: Sequence[int], rank: int, sched=None,
                  step: Optional[Callable] = None, norm2: Optional[Callable] = None,
                  finalize: Optional[Callable] = None, exchange: Optional[Callable] = None,
-                 renumber: bool = True, index32: bool = False):
+                 renumber: bool = True, index32: Optional[bool] = None):
         import torch
 
         self.torch = torch
@@ -158,7 +160,13 @@ class PowerIteration:
             raise ValueError("indptr has %d entries for a %d-row shard" % (indptr.numel(), self.rows))
         self.indptr = indptr
         gpu = step is None and norm2 is None and finalize is None and getattr(indices, "is_cuda", False)
-        if index32 and not (gpu and renumber and self.parts * self.stride < 2 ** 31):
+        fits = gpu and renumber and self.parts * self.stride < 2 ** 31
+        if index32 is None:
+            s0 = sched if sched is not None else None
+            split = getattr(s0, "split", 0) if s0 is not None else 0
+            vec = getattr(s0, "vector_width", 4) if s0 is not None else 4
+            index32 = fits and split == 0 and vec == 4
+        if index32 and not fits:
             raise ValueError("index32 needs the GPU steps, renumber=True and a padded layout below 2^31")
         self.index32 = bool(index32)
         self.indices = (renumber_columns(indices, self.bounds, self.stride, self.index32) if renumber else indices)
@@ -198,8 +206,9 @@ class PowerIteration:
     # -- GPU implementations -----------------------------------------------------------
     def _default_sched(self):
         s = self._lib.default_schedule()
-        # the fastest power-step schedule measured on the 8M-row uniform matrix
-        s.threads_per_row, s.unroll, s.vector_width, s.block_size, s.tile = 4, 2, 2, 256, 32
+        # the fastest power-step schedule measured on the 8M-row uniform matrix (with int32
+        # renumbered indices, chosen by default for it)
+        s.threads_per_row, s.unroll, s.vector_width, s.block_size, s.tile = 4, 1, 4, 256, 32
         s.split = self._lib.TG_SPLIT_ROWWISE
         return s
 
