@@ -395,9 +395,11 @@ def test_workspace_too_small_is_an_error():
     assert st == lib.TG_ENOMEM and "workspace" in lib.last_error()
 
 
-@pytest.mark.parametrize("split", ["rowwise", "merge"])
-def test_c5_spmm_sddmm_scaled(split):
-    m = M.baseline_matrix("c5", scale=0.05).astype(np.float32)
+@pytest.mark.parametrize("split,scale", [("rowwise", 0.05), ("merge", 0.05), ("merge", 0.3)])
+def test_c5_spmm_sddmm_scaled(split, scale):
+    """C5's generator at 5 % and 30 % of its rows (300k rows, ~4.8M nonzeros at 0.3), every
+    output element against the oracle (fp32 bar)."""
+    m = M.baseline_matrix("c5", scale=scale).astype(np.float32)
     rng = np.random.default_rng(8)
     B = rng.uniform(-1, 1, (m.cols, 128)).astype(np.float32)
     U = rng.uniform(-1, 1, (m.rows, 64)).astype(np.float32)
