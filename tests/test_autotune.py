@@ -43,7 +43,7 @@ def test_illegal_rules():
 def test_split_dimension():
     legal = at.legal_configs(at.B200_SEARCH_SPACE, at.SPLITS)
     assert {c.split for c in legal} == set(at.SPLITS)
-    assert len(legal) == 3 * len(at.legal_configs(at.B200_SEARCH_SPACE))
+    assert len(legal) == len(at.SPLITS) * len(at.legal_configs(at.B200_SEARCH_SPACE))
     # distinct hashes: a rowwise config keeps the reference's key, the others differ
     hashes = {c.hash() for c in legal}
     assert len(hashes) == len(legal)
@@ -55,9 +55,12 @@ def test_candidates_start_at_baseline(mode):
     assert c[0].hash() == at.BASELINE.hash()
     assert len(c) == 12 and len({x.hash() for x in c}) == 12
     assert all(at.illegal_reason(x) is None for x in c)
-    # no stream variants for SpMM (its stream split is the merge kernel)
+    # no stream variants for SpMM (its stream split is the merge kernel), no block variants
+    # outside SpMM (the block split is an SpMM mapping)
     d = at._candidate_configs(200, "random", random.Random(1), "spmm", at.SPLITS, dtype="f32")
     assert all(x.split != "stream" and x.dtype == "f32" for x in d)
+    assert any(x.split == "block" for x in d)
+    assert all(x.split != "block" for x in at._candidate_configs(200, "random", random.Random(1), "spmv", at.SPLITS))
 
 
 def test_coordinate_adds_split_variants():

@@ -71,12 +71,15 @@ SEARCH_SPACE: Dict[str, List[int]] = {
 B200_SEARCH_SPACE: Dict[str, List[int]] = dict(SEARCH_SPACE, threads_per_row=[1, 2, 4, 8, 16, 32])
 
 # Row mappings of the b200 kernels ("stream" is a distinct kernel only for SpMV).
-SPLITS: Tuple[str, ...] = ("rowwise", "merge", "stream")
+SPLITS: Tuple[str, ...] = ("rowwise", "merge", "stream", "block")
 
 BASELINE = Config(tile_size=32, threads_per_row=1, unroll=1, vector_width=1, block_size=128)
 
 _SUPPORTED_TPR = (1, 2, 4, 8, 16, 32)
 _STREAM_KERNELS = ("spmv", "fused_spmv_axpy")
+# the block split (row groups sharing a column list) is an SpMM mapping; elsewhere it
+# would repeat the merge split's candidates
+_BLOCK_KERNELS = ("spmm",)
 
 
 def illegal_reason(cfg: Config) -> Optional[str]:
@@ -233,7 +236,8 @@ def _candidate_configs(budget: int, mode: str, rng: random.Random, kernel: str =
     the baseline is always first.  Stream variants are kept only for the SpMV kernels
     (for SpMM/SDDMM the stream split is the merge kernel)."""
     space = space or SEARCH_SPACE
-    splits = [s for s in splits if s != "stream" or kernel in _STREAM_KERNELS]
+    splits = [s for s in splits if (s != "stream" or kernel in _STREAM_KERNELS) and
+              (s != "block" or kernel in _BLOCK_KERNELS)]
     base = Config(**dict(BASELINE.to_dict(), dtype=dtype))
     if mode == "coordinate":
         best = base
