@@ -80,8 +80,9 @@ def parse():
                     help="c4: the power-iteration headline (default); c1/c2/c3: one SpMV per step; "
                          "c5-spmm / c5-sddmm: one SpMM (K=128) / SDDMM (K=64) per step, fp32")
     ap.add_argument("--split", choices=["stream", "rowwise", "merge", "block"], default=None)
-    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
-                    help="N>1: fused SpMV + peer-memory push (p2p) or NCCL all-gather")
+    ap.add_argument("--exchange", choices=["p2p", "ce", "nccl"], default="p2p",
+                    help="N>1: fused SpMV + peer-memory push (p2p), plain step + one copy-engine copy per peer "
+                         "(ce), or NCCL all-gather")
     ap.add_argument("--tpr", type=int, default=None)
     ap.add_argument("--unroll", type=int, default=None)
     ap.add_argument("--vec", type=int, default=None)
@@ -282,8 +283,9 @@ def workload_config(n: int, world: int, exchange: str = "p2p"):
             "rows": n, "nnz": n * C4_PER_ROW, "iterations_per_step": ITERS,
             "parallelism": ("single GPU, no exchange" if world == 1 else
                             "row-sharded x%d, x replicated (%s)" % (
-                                world, "fused SpMV + peer-memory push of shards" if exchange == "p2p" else
-                                "in-place NCCL all-gather of shards")),
+                                world, {"p2p": "fused SpMV + peer-memory push of shards",
+                                        "ce": "SpMV, then one copy-engine copy of the shard per peer",
+                                        "nccl": "in-place NCCL all-gather of shards"}[exchange])),
             "l2": "inputs (%.2f GB) larger than L2 (126 MB): no flush" % (spmv_bytes(n, n, n * C4_PER_ROW) / 1e9)}
 
 
@@ -889,8 +891,9 @@ def main():
     d_x0 = h_x0.to(dev)
     i32 = args.index_bits == 32 and args.split != "stream"
     pi = PowerIteration(d_ip, d_ix, d_d, bounds, rank, sched=s, index32=i32)
-    if world > 1 and args.exchange == "p2p":
+    if world > 1 and args.exchange in ("p2p", "ce"):
         pi.p2p_connect()
+        pi.p2p_mode = "ce" if args.exchange == "ce" else "store"
     del d_ix
     x_out = torch.empty(r1 - r0, dtype=torch.float64, device=dev)
     lam = torch.empty(1, dtype=torch.float64, device=dev)
@@ -982,8 +985,9 @@ def main():
         dd = h_d.to(dev, non_blocking=True)
         xx = h_x0.to(dev, non_blocking=True)
         pe = PowerIteration(ip, ix, dd, bounds, rank, sched=s, index32=i32)
-        if world > 1 and args.exchange == "p2p":
+        if world > 1 and args.exchange in ("p2p", "ce"):
             pe.p2p_attach(pi.exchange_state)  # the mappings do not depend on the matrix
+            pe.p2p_mode = pi.p2p_mode
         del ix
         pe.set_x0(xx)
         pe.iterate(args.iters)

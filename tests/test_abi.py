@@ -18,7 +18,7 @@ def test_library_loads_and_reports_version():
 
 def test_every_header_symbol_is_exported_and_typed():
     declared = set(lib.header_symbols())
-    assert len(declared) == 48
+    assert len(declared) == 49
     assert declared == set(lib.SIGNATURES)
     out = subprocess.run(["nm", "-D", "--defined-only", lib.lib_path()], capture_output=True, text=True).stdout
     exported = {line.split()[-1] for line in out.splitlines() if " T " in line}

@@ -45,8 +45,9 @@ def _worker(rank, world, port, mode, q):
         pi = PowerIteration(torch.as_tensor(sh.indptr).to(dev), torch.as_tensor(sh.indices).to(dev),
                             torch.as_tensor(sh.data).to(dev), bounds, rank, sched=s)
         assert pi.index32 == (mode == "p2p-v4")
-        if mode.startswith("p2p"):
+        if mode.startswith("p2p") or mode == "ce":
             pi.p2p_connect()
+            pi.p2p_mode = "ce" if mode == "ce" else "store"
         x0 = np.random.default_rng(3).uniform(-1, 1, N_ROWS)
         res = []
         for _ in range(2):  # twice: the second solve reuses buffers, flags and epochs
@@ -55,8 +56,8 @@ def _worker(rank, world, port, mode, q):
             x, lam = pi.result()
             torch.cuda.synchronize()
             res.append((x.cpu().numpy(), float(lam[0])))
-        err = pi.error_word() if mode.startswith("p2p") else 0
-        if mode.startswith("p2p"):
+        err = pi.error_word() if mode != "nccl" else 0
+        if mode != "nccl":
             pi.close()
         q.put((rank, res, err))
         dist.barrier()
@@ -64,7 +65,7 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["nccl", "p2p", "p2p-v4"])
+@pytest.mark.parametrize("mode", ["nccl", "p2p", "p2p-v4", "ce"])
 def test_power_iteration_two_gpus(mode):
     world = min(torch.cuda.device_count(), 2)
     if world < 2:

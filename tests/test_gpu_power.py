@@ -107,9 +107,10 @@ def test_power_step_is_deterministic(split):
     assert np.array_equal(outs[0], outs[1])
 
 
+@pytest.mark.parametrize("mode", ["store", "ce"])
 @pytest.mark.parametrize("vec", [2, 4])
 @pytest.mark.parametrize("parts", [2, 3, 8])
-def test_p2p_fused_step_emulated_on_one_gpu(parts, vec):
+def test_p2p_fused_step_emulated_on_one_gpu(parts, vec, mode):
     """tg_power_step_p2p_f64 with every rank's buffers on one device: per epoch the
     ranks' kernels run one after another on one stream, so each wait is already met when
     its kernel starts (nothing waits on a kernel that has not run).  Checks the pushes
@@ -130,6 +131,7 @@ def test_p2p_fused_step_emulated_on_one_gpu(parts, vec):
     flags = [torch.zeros(parts, dtype=torch.int64, device=dev) for _ in range(parts)]
     for pi in pis:
         pi.p2p_setup([(q.x[0], q.x[1]) for q in pis], flags)
+        pi.p2p_mode = mode
     stride = pis[0].stride
     x0 = np.random.default_rng(2).uniform(-1, 1, n)
     for r, pi in enumerate(pis):

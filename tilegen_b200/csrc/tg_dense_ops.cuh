@@ -274,10 +274,7 @@ __global__ void __launch_bounds__(512) sddmm_kernel(DenseArgs<T> a) {
                     const int64_t col = kb + ((int64_t)lane + (int64_t)m * G) * VEC;
                     if (q0 + u < ce && col < a.kt) {
                         const Vec<T, VEC> vv = ld_gather_vec<T, VEC>(a.B + cidx[u] * a.ld + col, pg);
-                        // U[i] serves only the nonzeros of row i, walked back to back
-                        // (L1 keeps it); evict_first leaves L2 to the V rows, which are
-                        // reused across the whole call
-                        const Vec<T, VEC> uu = ld_gather_vec<T, VEC>(a.U + crow[u] * a.ld + col, ps);
+                        const Vec<T, VEC> uu = ld_gather_vec<T, VEC>(a.U + crow[u] * a.ld + col, pg);
 #pragma unroll
                         for (int e = 0; e < VEC; ++e) dot[u].mad(uu.v[e], vv.v[e]);
                     }

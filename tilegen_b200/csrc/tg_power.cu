@@ -14,6 +14,8 @@
 // a fixed row order, a fixed block tree, one partial per CTA, and the last CTA to arrive
 // (atomic ticket) adds the partials in CTA order.  No separate norm or scale pass.
 #include <algorithm>
+#include <mutex>
+#include <vector>
 
 #include "tg_rowdot.cuh"
 
@@ -482,6 +484,96 @@ int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, i
 }
 
 size_t power_err_offset() { return sizeof(double) * kPowerMaxGrid + 8; }
+
+// ------------------------------------------------------------- copy-engine exchange
+// The exchange as copies instead of stores from the computing warps: the plain power step
+// writes this rank's shard (and slot) into its own next-iterate buffer; one copy per peer
+// then moves the shard into that peer's buffer (copy engines, over NVLink), all copies
+// concurrent on internal side streams and joined back into the caller's stream; then a
+// one-warp kernel release-stores `epoch` into every rank's flag array.  The caller waits
+// (tg_p2p_wait, bounded) for the previous epoch before each step, so the next step reads a
+// complete iterate and nobody overwrites a buffer that is still being read.
+struct FlagArgs {
+    unsigned long long* f[8];
+    int nparts;
+    int rank;
+    unsigned long long epoch;
+};
+
+__global__ void p2p_release_kernel(FlagArgs a) {
+    __threadfence_system();
+    if ((int)threadIdx.x < a.nparts) st_release_sys(&a.f[threadIdx.x][a.rank], a.epoch);
+}
+
+namespace {
+
+struct SideStreams {
+    bool ready = false;
+    cudaStream_t s[8] = {};
+    cudaEvent_t fork = nullptr;
+    cudaEvent_t join[8] = {};
+};
+std::mutex g_side_mu;
+std::vector<SideStreams> g_side;  // per device, created on first use, kept for the process
+
+int side_streams(SideStreams** out) {
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc != TG_OK) return rc;
+    std::lock_guard<std::mutex> lk(g_side_mu);
+    if ((int)g_side.size() <= dev) g_side.resize(dev + 1);
+    SideStreams& ss = g_side[dev];
+    if (!ss.ready) {
+        rc = check_cuda(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming), "cudaEventCreate");
+        for (int k = 0; k < 8 && rc == TG_OK; ++k) {
+            rc = check_cuda(cudaStreamCreateWithFlags(&ss.s[k], cudaStreamNonBlocking), "cudaStreamCreate");
+            if (rc == TG_OK) rc = check_cuda(cudaEventCreateWithFlags(&ss.join[k], cudaEventDisableTiming), "cudaEventCreate");
+        }
+        if (rc != TG_OK) return rc;
+        ss.ready = true;
+    }
+    *out = &ss;
+    return TG_OK;
+}
+
+}  // namespace
+
+int power_push_run(double* const* y_peers, int nparts, int rank, int64_t stride, unsigned long long* const* flag_peers,
+                   unsigned long long epoch, cudaStream_t st) {
+    if (nparts < 1 || nparts > 8 || rank < 0 || rank >= nparts || stride < 1 || epoch < 1)
+        return set_error(TG_EINVAL, "power push: bad nparts/rank/stride/epoch (%d, %d, %lld)", nparts, rank,
+                         (long long)stride);
+    FlagArgs fa{};
+    for (int q = 0; q < nparts; ++q) {
+        if (!y_peers[q] || !flag_peers[q]) return set_error(TG_EINVAL, "power push: null peer pointer %d", q);
+        fa.f[q] = flag_peers[q];
+    }
+    fa.nparts = nparts;
+    fa.rank = rank;
+    fa.epoch = epoch;
+    if (nparts > 1) {
+        SideStreams* ss = nullptr;
+        int rc = side_streams(&ss);
+        if (rc != TG_OK) return rc;
+        rc = check_cuda(cudaEventRecord(ss->fork, st), "cudaEventRecord");
+        const double* src = y_peers[rank] + (int64_t)rank * stride;
+        int k = 0;
+        for (int q = 0; q < nparts && rc == TG_OK; ++q) {
+            if (q == rank) continue;
+            rc = check_cuda(cudaStreamWaitEvent(ss->s[k], ss->fork, 0), "cudaStreamWaitEvent");
+            if (rc == TG_OK)
+                rc = check_cuda(cudaMemcpyAsync(y_peers[q] + (int64_t)rank * stride, src, sizeof(double) * stride,
+                                                cudaMemcpyDefault, ss->s[k]),
+                                "cudaMemcpyAsync(peer shard)");
+            if (rc == TG_OK) rc = check_cuda(cudaEventRecord(ss->join[k], ss->s[k]), "cudaEventRecord");
+            if (rc == TG_OK) rc = check_cuda(cudaStreamWaitEvent(st, ss->join[k], 0), "cudaStreamWaitEvent");
+            ++k;
+        }
+        if (rc != TG_OK) return rc;
+    }
+    p2p_release_kernel<<<1, 32, 0, st>>>(fa);
+    return check_launch("p2p_release_kernel");
+}
 
 int p2p_wait_run(const unsigned long long* flag_local, int nparts, unsigned long long epoch, void* ws,
                  size_t ws_bytes, cudaStream_t st) {

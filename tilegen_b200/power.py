@@ -182,6 +182,10 @@ class PowerIteration:
         self._exchange = exchange or (self._nccl_exchange if self.parts > 1 else (lambda x: None))
         self.kernel_launches = 0
         self.p2p = False
+        # exchange over peer memory: "store" (tg_power_step_p2p_f64: the computing warps
+        # store every finished tile into every rank) or "ce" (tg_power_push_f64: the plain
+        # step, then one copy-engine copy of the shard per peer)
+        self.p2p_mode = "store"
         self._ex = None
         if step is None or norm2 is None or finalize is None:
             from . import lib as _lib
@@ -328,7 +332,12 @@ class PowerIteration:
         self.p2p = False
 
     def p2p_step(self, src_index: int) -> None:
-        """One fused step: read self.x[src_index], push into every rank's other buffer."""
+        """One exchanged step: read self.x[src_index], and deliver this rank's shard of the
+        result into every rank's other buffer (fused stores, or copies with
+        ``p2p_mode == "ce"``)."""
+        if self.p2p_mode == "ce":
+            self._ce_step(src_index)
+            return
         L = self._lib.load()
         ex = self._ex
         ex.epoch += 1
@@ -336,6 +345,20 @@ class PowerIteration:
                                                 self.rank, self.stride, ex.y_ptrs[1 - src_index], ex.flag_ptrs,
                                                 ex.epoch, ctypes.byref(self._sched_c), self.ws.data_ptr(),
                                                 self.ws.numel(), self._stream()), "tg_power_step_p2p_f64")
+        self.kernel_launches += 1
+
+    def _ce_step(self, src_index: int) -> None:
+        L = self._lib.load()
+        ex = self._ex
+        st = self._stream()
+        if ex.epoch > 0:  # every rank has delivered the previous epoch (bounded wait)
+            self._lib.check(L.tg_p2p_wait(ex.flags_local.data_ptr(), self.parts, ex.epoch, self.ws.data_ptr(),
+                                          self.ws.numel(), st), "tg_p2p_wait")
+            self.kernel_launches += 1
+        ex.epoch += 1
+        self._gpu_step(self.x[src_index], self.shard(self.x[1 - src_index]))
+        self._lib.check(L.tg_power_push_f64(ex.y_ptrs[1 - src_index], self.parts, self.rank, self.stride,
+                                            ex.flag_ptrs, ex.epoch, st), "tg_power_push_f64")
         self.kernel_launches += 1
 
     def p2p_wait(self) -> None:
