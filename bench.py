@@ -83,6 +83,7 @@ def parse():
     ap.add_argument("--exchange", choices=["p2p", "ce", "nccl"], default="p2p",
                     help="N>1: fused SpMV + peer-memory push (p2p), plain step + one copy-engine copy per peer "
                          "(ce), or NCCL all-gather")
+    ap.add_argument("--ce-chunks", type=int, default=4, help="--exchange ce: row chunks per step (1-16)")
     ap.add_argument("--tpr", type=int, default=None)
     ap.add_argument("--unroll", type=int, default=None)
     ap.add_argument("--vec", type=int, default=None)
@@ -894,6 +895,7 @@ def main():
     if world > 1 and args.exchange in ("p2p", "ce"):
         pi.p2p_connect()
         pi.p2p_mode = "ce" if args.exchange == "ce" else "store"
+        pi.ce_chunks = args.ce_chunks
     del d_ix
     x_out = torch.empty(r1 - r0, dtype=torch.float64, device=dev)
     lam = torch.empty(1, dtype=torch.float64, device=dev)
@@ -988,6 +990,7 @@ def main():
         if world > 1 and args.exchange in ("p2p", "ce"):
             pe.p2p_attach(pi.exchange_state)  # the mappings do not depend on the matrix
             pe.p2p_mode = pi.p2p_mode
+            pe.ce_chunks = pi.ce_chunks
         del ix
         pe.set_x0(xx)
         pe.iterate(args.iters)

@@ -219,15 +219,18 @@ TG_API int tg_power_step_p2p_f64(const tg_csr* A, const double* x, int32_t npart
                                  int64_t stride, double* const* y_peers, uint64_t* const* flag_peers,
                                  uint64_t epoch, const tg_sched* s, void* workspace,
                                  size_t workspace_bytes, tg_stream_t stream);
-/* The exchange by copy engines (the alternative to tg_power_step_p2p_f64): after
- * tg_power_step_f64 wrote this rank's shard and slot into its own next-iterate buffer
- * y_peers[rank] (at rank * stride), copy that shard into every other rank's buffer (one
- * copy per peer, concurrent, on side streams the library keeps per device, joined back into
- * `stream`), then release-store `epoch` into flag_peers[q][rank] for every q.  Before the
- * next step on the same buffers, tg_p2p_wait(flag_local, nparts, epoch, ...) (bounded).
- * Peer buffers and flags as for tg_power_step_p2p_f64. */
-TG_API int tg_power_push_f64(double* const* y_peers, int32_t nparts, int32_t rank, int64_t stride,
-                             uint64_t* const* flag_peers, uint64_t epoch, tg_stream_t stream);
+/* The power step with the exchange done by copy engines (the alternative to
+ * tg_power_step_p2p_f64; same peer buffers, flags and epochs): wait (bounded, 2 s) until
+ * every rank released epoch - 1; compute this rank's rows in `nchunks` (1..16) row chunks
+ * into its own next-iterate buffer y_peers[rank], copying each chunk into every other
+ * rank's buffer as soon as it is done (one copy per peer, on side streams the library keeps
+ * per device, so the copies overlap the next chunk's compute); the slot (the chunks' sums
+ * of squares added in chunk order) travels with the last chunk; then release `epoch` into
+ * flag_peers[q][rank] for every q.  One call at a time per device (the side streams are
+ * shared).  Rowwise split only; TG_FLAG_INDEX32 as for tg_power_step_f64. */
+TG_API int tg_power_step_ce_f64(const tg_csr* A, const double* x, int32_t nparts, int32_t rank, int64_t stride,
+                                double* const* y_peers, uint64_t* const* flag_peers, uint64_t epoch, int32_t nchunks,
+                                const tg_sched* s, void* workspace, size_t workspace_bytes, tg_stream_t stream);
 /* Copies the power workspace's error word to *err (synchronises `stream`): 16 = a peer
  * wait ran out.  Zero when nothing went wrong. */
 TG_API int tg_power_error(const void* workspace, uint32_t* err, tg_stream_t stream);

@@ -107,7 +107,7 @@ def test_power_step_is_deterministic(split):
     assert np.array_equal(outs[0], outs[1])
 
 
-@pytest.mark.parametrize("mode", ["store", "ce"])
+@pytest.mark.parametrize("mode", ["store", "ce", "ce1"])
 @pytest.mark.parametrize("vec", [2, 4])
 @pytest.mark.parametrize("parts", [2, 3, 8])
 def test_p2p_fused_step_emulated_on_one_gpu(parts, vec, mode):
@@ -131,7 +131,8 @@ def test_p2p_fused_step_emulated_on_one_gpu(parts, vec, mode):
     flags = [torch.zeros(parts, dtype=torch.int64, device=dev) for _ in range(parts)]
     for pi in pis:
         pi.p2p_setup([(q.x[0], q.x[1]) for q in pis], flags)
-        pi.p2p_mode = mode
+        pi.p2p_mode = "store" if mode == "store" else "ce"
+        pi.ce_chunks = 1 if mode == "ce1" else 4
     stride = pis[0].stride
     x0 = np.random.default_rng(2).uniform(-1, 1, n)
     for r, pi in enumerate(pis):

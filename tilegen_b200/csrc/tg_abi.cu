@@ -62,8 +62,9 @@ int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, i
                        double* const* y_peers, unsigned long long* const* flag_peers, unsigned long long epoch,
                        const tg_sched& s, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t power_err_offset();
-int power_push_run(double* const* y_peers, int nparts, int rank, int64_t stride, unsigned long long* const* flag_peers,
-                   unsigned long long epoch, cudaStream_t st);
+int power_step_ce_run(const tg_csr& A, const double* x, int nparts, int rank, int64_t stride, double* const* y_peers,
+                      unsigned long long* const* flag_peers, unsigned long long epoch, int nchunks, const tg_sched& s,
+                      void* ws, size_t ws_bytes, cudaStream_t st);
 int p2p_wait_run(const unsigned long long* flag_local, int nparts, unsigned long long epoch, void* ws,
                  size_t ws_bytes, cudaStream_t st);
 
@@ -425,11 +426,13 @@ int tg_power_error(const void* workspace, uint32_t* err, tg_stream_t stream) {
     return check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize");
 }
 
-int tg_power_push_f64(double* const* y_peers, int32_t nparts, int32_t rank, int64_t stride, uint64_t* const* flag_peers,
-                      uint64_t epoch, tg_stream_t stream) {
-    if (!y_peers || !flag_peers) return set_error(TG_EINVAL, "tg_power_push_f64: null pointer");
-    return power_push_run(y_peers, nparts, rank, stride, reinterpret_cast<unsigned long long* const*>(flag_peers),
-                          epoch, static_cast<cudaStream_t>(stream));
+int tg_power_step_ce_f64(const tg_csr* A, const double* x, int32_t nparts, int32_t rank, int64_t stride,
+                         double* const* y_peers, uint64_t* const* flag_peers, uint64_t epoch, int32_t nchunks,
+                         const tg_sched* s, void* workspace, size_t workspace_bytes, tg_stream_t stream) {
+    TG_PRELUDE("tg_power_step_ce_f64");
+    if (!x || !y_peers || !flag_peers) return set_error(TG_EINVAL, "tg_power_step_ce_f64: null pointer");
+    return power_step_ce_run(*A, x, nparts, rank, stride, y_peers, reinterpret_cast<unsigned long long* const*>(flag_peers),
+                             epoch, nchunks, sc, workspace, workspace_bytes, st);
 }
 
 int tg_power_clear_error(void* workspace, tg_stream_t stream) {

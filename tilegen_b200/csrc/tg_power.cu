@@ -28,11 +28,12 @@ struct PowerArgs {
     const double* x;  // padded input iterate, nparts * stride
     int nparts;
     int64_t stride;
-    double* y;  // output shard (stride doubles, slot at stride-1)
+    double* y;  // output rows (the shard, or a chunk of its rows)
     int64_t rows;
     int64_t rows_per_tile;
     double* partials;  // [gridDim.x]
     unsigned* ticket;  // [1], zero between launches
+    double* slot_out;  // where sum(y^2) goes: the shard's slot, or a chunk's partial
 };
 
 // Deterministic sum of per-thread values of one CTA (fixed shuffle tree, warps in order).
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(512) power_step_kernel(PowerArgs a) {
         }
     }
     const double part = block_sum(sq, s_warp);
-    grid_sum_last(part, a.partials, a.ticket, a.y + a.stride - 1);
+    grid_sum_last(part, a.partials, a.ticket, a.slot_out);
 }
 
 // ------------------------------------------------------------------ fused exchange
@@ -377,6 +378,9 @@ size_t power_ws_bytes(int64_t nnz, const tg_sched& s) {
     return b;
 }
 
+int power_rows_run(const tg_csr& A, int64_t row0, int64_t row1, const double* x, int nparts, int64_t stride,
+                   double* y, double* slot_out, const tg_sched& s, void* ws, cudaStream_t st);
+
 int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride, double* y, const tg_sched& s,
                    void* ws, size_t ws_bytes, cudaStream_t st) {
     if (nparts < 1 || stride < A.rows + 1)
@@ -396,9 +400,14 @@ int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride,
     }
     if (ws == nullptr || ws_bytes < power_ws_bytes_impl())
         return set_error(TG_ENOMEM, "power step needs %zu workspace bytes, got %zu", power_ws_bytes_impl(), ws_bytes);
-    if (nparts < 1 || stride < A.rows + 1)
-        return set_error(TG_EINVAL, "power step: need nparts >= 1 and stride >= rows + 1 (nparts=%d stride=%lld)",
-                         nparts, (long long)stride);
+    return power_rows_run(A, 0, A.rows, x, nparts, stride, y, y + stride - 1, s, ws, st);
+}
+
+// Rows [row0, row1) of the shard A (its indptr is absolute into indices/data), written to
+// y[row0, row1), sum of their squares to *slot_out; the rowwise power-step kernel.
+int power_rows_run(const tg_csr& A, int64_t row0, int64_t row1, const double* x, int nparts, int64_t stride,
+                   double* y, double* slot_out, const tg_sched& s, void* ws, cudaStream_t st) {
+    const bool i32 = index32(s);
     const int tpr = s.threads_per_row < 4 ? 4 : s.threads_per_row;
     const int u = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
     int v = s.vector_width;
@@ -406,18 +415,19 @@ int power_step_run(const tg_csr& A, const double* x, int nparts, int64_t stride,
     const int threads = s.block_size;
     PowerWs w = carve(ws);
     PowerArgs a{};
-    a.indptr = A.indptr;
+    a.indptr = A.indptr + row0;
     a.indices = A.indices;
     a.data = static_cast<const double*>(A.data);
     a.x = x;
     a.nparts = nparts;
     a.stride = stride;
-    a.y = y;
-    a.rows = A.rows;
+    a.y = y + row0;
+    a.rows = row1 - row0;
     a.rows_per_tile = std::max<int64_t>(s.tile, threads / tpr);
     a.partials = w.partials;
     a.ticket = w.ticket;
-    int64_t blocks = ceil_div(std::max<int64_t>(A.rows, 1), a.rows_per_tile);
+    a.slot_out = slot_out;
+    int64_t blocks = ceil_div(std::max<int64_t>(a.rows, 1), a.rows_per_tile);
     blocks = std::min<int64_t>(blocks, kPowerMaxGrid);
     if (!power_dispatch(tpr, u, v, a, i32, (int)blocks, threads, st))
         return set_error(TG_EUNSUPPORTED, "no power-step instance for TPR=%d U=%d V=%d", tpr, u, v);
@@ -486,13 +496,14 @@ int power_step_p2p_run(const tg_csr& A, const double* x, int nparts, int rank, i
 size_t power_err_offset() { return sizeof(double) * kPowerMaxGrid + 8; }
 
 // ------------------------------------------------------------- copy-engine exchange
-// The exchange as copies instead of stores from the computing warps: the plain power step
-// writes this rank's shard (and slot) into its own next-iterate buffer; one copy per peer
-// then moves the shard into that peer's buffer (copy engines, over NVLink), all copies
-// concurrent on internal side streams and joined back into the caller's stream; then a
-// one-warp kernel release-stores `epoch` into every rank's flag array.  The caller waits
-// (tg_p2p_wait, bounded) for the previous epoch before each step, so the next step reads a
-// complete iterate and nobody overwrites a buffer that is still being read.
+// The exchange as copies instead of stores from the computing warps: the power step writes
+// this rank's rows (and slot) into its own next-iterate buffer; copies (copy engines, over
+// NVLink) move them into every peer's buffer, one side stream per peer, joined back into
+// the caller's stream; then a one-warp kernel release-stores `epoch` into every rank's
+// flag array.  Each step first waits (bounded) for the previous epoch, so it reads a
+// complete iterate and nobody overwrites a buffer that is still being read.  Kernels on
+// one GPU never wait for one another: the wait is for flags other GPUs release, and the
+// release of this GPU comes after its copies in stream order.
 struct FlagArgs {
     unsigned long long* f[8];
     int nparts;
@@ -538,36 +549,89 @@ int side_streams(SideStreams** out) {
 
 }  // namespace
 
-int power_push_run(double* const* y_peers, int nparts, int rank, int64_t stride, unsigned long long* const* flag_peers,
-                   unsigned long long epoch, cudaStream_t st) {
-    if (nparts < 1 || nparts > 8 || rank < 0 || rank >= nparts || stride < 1 || epoch < 1)
-        return set_error(TG_EINVAL, "power push: bad nparts/rank/stride/epoch (%d, %d, %lld)", nparts, rank,
+// slot <- parts[0] + parts[1] + ... in that order (the chunks' sums of squares).
+__global__ void slot_combine_kernel(const double* parts, int n, double* slot) {
+    double t = 0.0;
+    for (int k = 0; k < n; ++k) t += parts[k];
+    *slot = t;
+}
+
+constexpr int kMaxChunks = 16;
+
+// chunk partial slots: inside the norm region, after the ticket and the error word
+double* chunk_slots(void* ws) {
+    return reinterpret_cast<double*>(static_cast<char*>(ws) + sizeof(double) * kPowerMaxGrid + 64);
+}
+
+int p2p_wait_run(const unsigned long long* flag_local, int nparts, unsigned long long epoch, void* ws,
+                 size_t ws_bytes, cudaStream_t st);
+
+// One iteration with the copy-engine exchange, pipelined over `nchunks` row chunks:
+// wait (bounded) until every rank delivered epoch-1; for each chunk, the power-step kernel
+// on its rows, then one copy of those rows to every peer on that peer's side stream, so
+// the copies of chunk k run while chunk k+1 computes; the chunks' sums of squares are
+// combined in chunk order into the slot, which travels with the last chunk; the copies are
+// joined back into `st` and `epoch` is released to every rank.
+int power_step_ce_run(const tg_csr& A, const double* x, int nparts, int rank, int64_t stride, double* const* y_peers,
+                      unsigned long long* const* flag_peers, unsigned long long epoch, int nchunks, const tg_sched& s,
+                      void* ws, size_t ws_bytes, cudaStream_t st) {
+    if (nparts < 1 || nparts > 8 || rank < 0 || rank >= nparts || stride < A.rows + 1 || epoch < 1)
+        return set_error(TG_EINVAL, "ce step: bad nparts/rank/stride/epoch (%d, %d, %lld)", nparts, rank,
                          (long long)stride);
+    if (nchunks < 1 || nchunks > kMaxChunks)
+        return set_error(TG_EINVAL, "ce step: nchunks must be in [1, %d] (got %d)", kMaxChunks, nchunks);
+    if (s.split == TG_SPLIT_STREAM) return set_error(TG_EUNSUPPORTED, "ce step: the rowwise split only");
+    if (ws == nullptr || ws_bytes < power_ws_bytes_impl())
+        return set_error(TG_ENOMEM, "ce step needs %zu workspace bytes", power_ws_bytes_impl());
     FlagArgs fa{};
     for (int q = 0; q < nparts; ++q) {
-        if (!y_peers[q] || !flag_peers[q]) return set_error(TG_EINVAL, "power push: null peer pointer %d", q);
+        if (!y_peers[q] || !flag_peers[q]) return set_error(TG_EINVAL, "ce step: null peer pointer %d", q);
         fa.f[q] = flag_peers[q];
     }
     fa.nparts = nparts;
     fa.rank = rank;
     fa.epoch = epoch;
+    int rc = TG_OK;
+    if (epoch > 1) rc = p2p_wait_run(flag_peers[rank], nparts, epoch - 1, ws, ws_bytes, st);
+    if (rc != TG_OK) return rc;
+    SideStreams* ss = nullptr;
     if (nparts > 1) {
-        SideStreams* ss = nullptr;
-        int rc = side_streams(&ss);
+        rc = side_streams(&ss);
         if (rc != TG_OK) return rc;
+    }
+    double* own = y_peers[rank] + (int64_t)rank * stride;
+    double* parts = chunk_slots(ws);
+    for (int k = 0; k < nchunks && rc == TG_OK; ++k) {
+        const int64_t r0 = A.rows * k / nchunks, r1 = A.rows * (k + 1) / nchunks;
+        rc = power_rows_run(A, r0, r1, x, nparts, stride, own, parts + k, s, ws, st);
+        const bool last = k == nchunks - 1;
+        if (rc == TG_OK && last) {
+            slot_combine_kernel<<<1, 1, 0, st>>>(parts, nchunks, own + stride - 1);
+            rc = check_launch("slot_combine_kernel");
+        }
+        if (rc != TG_OK || nparts == 1) continue;
+        const int64_t c0 = r0, c1 = last ? stride : r1;  // the last chunk carries the padding and the slot
+        if (c1 <= c0) continue;
         rc = check_cuda(cudaEventRecord(ss->fork, st), "cudaEventRecord");
-        const double* src = y_peers[rank] + (int64_t)rank * stride;
-        int k = 0;
+        int j = 0;
         for (int q = 0; q < nparts && rc == TG_OK; ++q) {
             if (q == rank) continue;
-            rc = check_cuda(cudaStreamWaitEvent(ss->s[k], ss->fork, 0), "cudaStreamWaitEvent");
+            rc = check_cuda(cudaStreamWaitEvent(ss->s[j], ss->fork, 0), "cudaStreamWaitEvent");
             if (rc == TG_OK)
-                rc = check_cuda(cudaMemcpyAsync(y_peers[q] + (int64_t)rank * stride, src, sizeof(double) * stride,
-                                                cudaMemcpyDefault, ss->s[k]),
-                                "cudaMemcpyAsync(peer shard)");
-            if (rc == TG_OK) rc = check_cuda(cudaEventRecord(ss->join[k], ss->s[k]), "cudaEventRecord");
-            if (rc == TG_OK) rc = check_cuda(cudaStreamWaitEvent(st, ss->join[k], 0), "cudaStreamWaitEvent");
-            ++k;
+                rc = check_cuda(cudaMemcpyAsync(y_peers[q] + (int64_t)rank * stride + c0, own + c0,
+                                                sizeof(double) * (c1 - c0), cudaMemcpyDefault, ss->s[j]),
+                                "cudaMemcpyAsync(peer rows)");
+            ++j;
+        }
+    }
+    if (rc != TG_OK) return rc;
+    if (nparts > 1) {
+        int j = 0;
+        for (int q = 0; q < nparts && rc == TG_OK; ++q) {
+            if (q == rank) continue;
+            rc = check_cuda(cudaEventRecord(ss->join[j], ss->s[j]), "cudaEventRecord");
+            if (rc == TG_OK) rc = check_cuda(cudaStreamWaitEvent(st, ss->join[j], 0), "cudaStreamWaitEvent");
+            ++j;
         }
         if (rc != TG_OK) return rc;
     }

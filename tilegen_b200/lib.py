@@ -136,7 +136,8 @@ SIGNATURES = {
     "tg_p2p_wait": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_uint64, _P, _SZ, _P]),
     "tg_power_error": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
     "tg_power_clear_error": (ctypes.c_int, [_P, _P]),
-    "tg_power_push_f64": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _I64, _P, ctypes.c_uint64, _P]),
+    "tg_power_step_ce_f64": (ctypes.c_int, [_CP, _P, ctypes.c_int32, ctypes.c_int32, _I64, _P, _P, ctypes.c_uint64,
+                                            ctypes.c_int32, _SP, _P, _SZ, _P]),
     "tg_peer_buffer_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(ctypes.c_void_p)]),
     "tg_peer_buffer_free": (ctypes.c_int, [_P]),
     "tg_ipc_get_handle": (ctypes.c_int, [_P, ctypes.c_char_p]),

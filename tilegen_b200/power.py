@@ -183,9 +183,11 @@ class PowerIteration:
         self.kernel_launches = 0
         self.p2p = False
         # exchange over peer memory: "store" (tg_power_step_p2p_f64: the computing warps
-        # store every finished tile into every rank) or "ce" (tg_power_push_f64: the plain
-        # step, then one copy-engine copy of the shard per peer)
+        # store every finished tile into every rank) or "ce" (tg_power_step_ce_f64: the
+        # step in row chunks, each chunk copied to every peer by the copy engines while
+        # the next one computes)
         self.p2p_mode = "store"
+        self.ce_chunks = 4  # "ce": row chunks whose copies overlap the next chunk's compute
         self._ex = None
         if step is None or norm2 is None or finalize is None:
             from . import lib as _lib
@@ -350,16 +352,13 @@ class PowerIteration:
     def _ce_step(self, src_index: int) -> None:
         L = self._lib.load()
         ex = self._ex
-        st = self._stream()
-        if ex.epoch > 0:  # every rank has delivered the previous epoch (bounded wait)
-            self._lib.check(L.tg_p2p_wait(ex.flags_local.data_ptr(), self.parts, ex.epoch, self.ws.data_ptr(),
-                                          self.ws.numel(), st), "tg_p2p_wait")
-            self.kernel_launches += 1
         ex.epoch += 1
-        self._gpu_step(self.x[src_index], self.shard(self.x[1 - src_index]))
-        self._lib.check(L.tg_power_push_f64(ex.y_ptrs[1 - src_index], self.parts, self.rank, self.stride,
-                                            ex.flag_ptrs, ex.epoch, st), "tg_power_push_f64")
-        self.kernel_launches += 1
+        self._lib.check(L.tg_power_step_ce_f64(ctypes.byref(self._desc), self.x[src_index].data_ptr(), self.parts,
+                                               self.rank, self.stride, ex.y_ptrs[1 - src_index], ex.flag_ptrs,
+                                               ex.epoch, self.ce_chunks, ctypes.byref(self._sched_c),
+                                               self.ws.data_ptr(), self.ws.numel(), self._stream()),
+                        "tg_power_step_ce_f64")
+        self.kernel_launches += self.ce_chunks + 2 + (1 if ex.epoch > 1 else 0)
 
     def p2p_wait(self) -> None:
         L = self._lib.load()
