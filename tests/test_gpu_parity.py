@@ -257,23 +257,6 @@ def test_dense_widths(K, split):
                 assert rel_err(out, ref) <= 1e-4, (kernel, K, split)
 
 
-@pytest.mark.parametrize("K,tpr", [(128, 32), (64, 16), (16, 4), (100, 32)])
-@pytest.mark.parametrize("split", ["rowwise", "merge"])
-def test_dense_eight_gathers_in_flight(K, tpr, split):
-    """SpMM / SDDMM with U = 8 (eight rows' gathers in flight per lane group, one column
-    vector per lane) against the oracle, fp64 and fp32."""
-    m = M.baseline_matrix("c3", scale=0.05)
-    data = inputs_for("spmm", m, K, 12)
-    for dtype in ("f64", "f32"):
-        cfg = cg.Config(threads_per_row=tpr, unroll=8, vector_width=4, split=split, dtype=dtype)
-        for kernel, ref in (("spmm", O.spmm(m, data[2])), ("sddmm", O.sddmm(m, data[3], data[4]))):
-            out = run_kernel(cg.generate(kernel, cfg), m, data, K=K)
-            if dtype == "f64":
-                check_f64(out, ref, m)
-            else:
-                assert rel_err(out, ref) <= 1e-4, (kernel, K, split)
-
-
 def _wide_matrix():
     """2000 rows over 1,000,000 columns (power-law row lengths, a few long rows): a dense
     operand of 1M rows, larger than L2 for every K here."""

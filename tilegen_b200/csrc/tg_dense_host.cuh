@@ -5,8 +5,7 @@
 //   TPR -> G, lanes per group (clamped to 4..32 and to the lanes the row width can use),
 //   V   -> VEC, elements per gather (largest of {4,2,1} <= V that divides K and the
 //          operand alignment; 2 at most for fp64),
-//   U   -> nonzeros whose gathers are in flight per group (1, 2, 4, or 8 where a lane holds
-//          one column vector),
+//   U   -> nonzeros whose gathers are in flight per group (1, 2 or 4),
 //   B   -> threads per CTA (128, 256 or 512),
 //   split / chunk_nnz -> rowwise (one group per row) or merge (one group per chunk);
 //          block (SpMM): a warp per group of kGroupRows rows sharing each gathered row;
@@ -70,7 +69,7 @@ DenseChoice choose_dense(const tg_sched& s, int64_t K, bool is_spmm, const void*
     // SpMM covers at most G*VEC*NCV columns per launch (its accumulators live in
     // registers); SDDMM loops over all K columns inside the kernel
     d.ktile = is_spmm ? std::min<int64_t>(K, (int64_t)g * vec * d.NCV) : K;
-    d.U = s.unroll >= 8 ? 8 : (s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1));
+    d.U = s.unroll >= 4 ? 4 : (s.unroll >= 2 ? 2 : 1);
     d.block = (s.block_size >= 512) ? 512 : (s.block_size >= 256 ? 256 : 128);
     d.merge = (s.split == TG_SPLIT_MERGE || s.split == TG_SPLIT_STREAM || s.split == TG_SPLIT_BLOCK);
     d.S = s.chunk_nnz > 0 ? s.chunk_nnz : default_dense_chunk(nnz, is_spmm);
@@ -104,9 +103,6 @@ bool dense_u(const DenseChoice& d, bool sp, const DenseArgs<T>& a, cudaStream_t 
         case 1: return dense_m<T, G, VEC, NCV, 1>(d, sp, a, st);
         case 2: return dense_m<T, G, VEC, NCV, 2>(d, sp, a, st);
         case 4: return dense_m<T, G, VEC, NCV, 4>(d, sp, a, st);
-        case 8:  // eight gathers in flight: instantiated for one column vector per lane only
-            if constexpr (NCV == 1) return dense_m<T, G, VEC, NCV, 8>(d, sp, a, st);
-            return dense_m<T, G, VEC, NCV, 4>(d, sp, a, st);
     }
     return false;
 }
