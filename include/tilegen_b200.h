@@ -59,7 +59,8 @@ typedef void* tg_stream_t;
 /* ------------------------------------------------------------------ schedule */
 /* Row-to-thread mapping of the kernels. */
 #define TG_SPLIT_ROWWISE 0 /* reference mapping: T rows per CTA tile, TPR lanes per row */
-#define TG_SPLIT_MERGE 1   /* nnz-balanced chunks, rows split across chunks + fix-up */
+#define TG_SPLIT_MERGE 1   /* nnz-balanced chunks; a row split across chunks is finished by
+                              its last contributor */
 #define TG_SPLIT_AUTO 2    /* library picks: the merge split (any row-length distribution) */
 #define TG_SPLIT_STREAM 3  /* SpMV: persistent TMA-fed row-block kernel; merge for SpMM/SDDMM */
 #define TG_SPLIT_BLOCK 4   /* SpMM: groups of 8 consecutive rows with one shared column list
