@@ -3,8 +3,8 @@
 // A CSR SpMV over uniformly scattered columns is bound by how fast the SMs can gather
 // 8-byte x values from random addresses (one 32-byte L2 sector per gather), not by the
 // HBM stream of indices and values.  This kernel performs the same gathers as the SpMV
-// -- the same column indices, the same load instruction and L2 policy (ld.global.nc
-// with evict_last), four gathers in flight per thread -- and nothing else (no values,
+// -- the same column indices, the same load instruction and cache policy (ld.global.nc,
+// no L1 allocation, L2 evict_last), four gathers in flight per thread -- and nothing else (no values,
 // no row offsets, no row reductions, no output vector), so the time it takes is the
 // floor for the SpMV's gather traffic on this GPU.  Benchmarks report the SpMV's time
 // against it next to the HBM roofline.
@@ -35,11 +35,11 @@ __global__ void __launch_bounds__(256) gather_probe_kernel(const I* __restrict__
     for (; i + 3 * T < n; i += 4 * T) {
         const int64_t c0 = ld_stream(idx + i, ps), c1 = ld_stream(idx + i + T, ps);
         const int64_t c2 = ld_stream(idx + i + 2 * T, ps), c3 = ld_stream(idx + i + 3 * T, ps);
-        const double g0 = ld_gather(x + c0, pg), g1 = ld_gather(x + c1, pg);
-        const double g2 = ld_gather(x + c2, pg), g3 = ld_gather(x + c3, pg);
+        const double g0 = ld_gather_na(x + c0, pg), g1 = ld_gather_na(x + c1, pg);
+        const double g2 = ld_gather_na(x + c2, pg), g3 = ld_gather_na(x + c3, pg);
         acc += (g0 + g1) + (g2 + g3);
     }
-    for (; i < n; i += T) acc += ld_gather(x + ld_stream(idx + i, ps), pg);
+    for (; i < n; i += T) acc += ld_gather_na(x + ld_stream(idx + i, ps), pg);
     acc = group_sum<kWarp>(acc, kFull);
     if ((threadIdx.x % kWarp) == 0) atomicAdd(out, acc);
 }

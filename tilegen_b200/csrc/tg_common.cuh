@@ -90,6 +90,14 @@ __device__ __forceinline__ double ld_gather(const double* p, uint64_t pol) {
     asm("ld.global.nc.L2::cache_hint.f64 %0, [%1], %2;" : "=d"(v) : "l"(p), "l"(pol));
     return v;
 }
+// The same gather without an L1 line: for an operand far larger than L1 whose elements are
+// not reused by the same SM (the power iteration's 64 MB iterate), allocating in L1 only
+// costs L1 tag work.
+__device__ __forceinline__ double ld_gather_na(const double* p, uint64_t pol) {
+    double v;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.f64 %0, [%1], %2;" : "=d"(v) : "l"(p), "l"(pol));
+    return v;
+}
 __device__ __forceinline__ float ld_gather(const float* p, uint64_t pol) {
     float v;
     asm("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));

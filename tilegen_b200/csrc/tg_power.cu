@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(512) power_step_kernel(PowerArgs a) {
          base += (int64_t)gridDim.x * a.rows_per_tile) {
         const int64_t end = min(base + a.rows_per_tile, a.rows);
         for (int64_t i = base + group; i < end; i += groups) {
-            double acc = row_dot<double, TPR, U, V, I>(indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
+            double acc = row_dot<double, TPR, U, V, I, true>(indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
             if constexpr (TPR > 1) acc = group_sum<TPR>(acc, mask);
             if (lane == 0) {
                 const double v = scale * acc;
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(256) power_p2p_kernel(PowerP2PArgs a) {
         const int64_t i = base + group;
         double v = 0.0;
         if (i < rows) {
-            double acc = row_dot<double, TPR, U, V, I>(indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
+            double acc = row_dot<double, TPR, U, V, I, true>(indices, a.data, a.x, a.indptr[i], a.indptr[i + 1], lane, ps, pg);
             if constexpr (TPR > 1) acc = group_sum<TPR>(acc, mask);
             v = scale * acc;
             if (lane == 0) sq = fma(v, v, sq);

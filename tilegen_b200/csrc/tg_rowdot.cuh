@@ -38,10 +38,21 @@ __device__ __forceinline__ void ld_stream_vec(const I* pi, const T* pv, uint64_t
     }
 }
 
+// x gather of row_dot: through L1 (default), or without allocating there (NA).
+template <bool NA, typename T>
+__device__ __forceinline__ T gather_x(const T* p, uint64_t pol) {
+    if constexpr (NA && sizeof(T) == 8) {
+        return ld_gather_na(p, pol);
+    } else {
+        return ld_gather(p, pol);
+    }
+}
+
 // Dot product of row [p, pe) with x by the TPR lanes of one group (this lane's share).
 // I is the column index type (int64_t, or int32_t for a matrix the caller renumbered to
-// 32-bit indices).
-template <typename T, int TPR, int U, int V, typename I = int64_t>
+// 32-bit indices); NA gathers x without L1 allocation (the power steps, whose x is 8M
+// doubles: measured 0.6 % faster there, 3.5 % slower on a 100k-column SpMV).
+template <typename T, int TPR, int U, int V, typename I = int64_t, bool NA = false>
 __device__ __forceinline__ T row_dot(const I* __restrict__ idx, const T* __restrict__ val,
                                      const T* __restrict__ x, int64_t p, int64_t pe, int lane, uint64_t ps,
                                      uint64_t pg) {
@@ -57,15 +68,15 @@ __device__ __forceinline__ T row_dot(const I* __restrict__ idx, const T* __restr
                 v[u] = ld_stream(val + q + u * TPR, ps);
             }
 #pragma unroll
-            for (int u = 0; u < U; ++u) acc.mad(v[u], ld_gather(x + c[u], pg));
+            for (int u = 0; u < U; ++u) acc.mad(v[u], gather_x<NA>(x + c[u], pg));
         }
-        for (; q < pe; q += TPR) acc.mad(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg));
+        for (; q < pe; q += TPR) acc.mad(ld_stream(val + q, ps), gather_x<NA>(x + ld_stream(idx + q, ps), pg));
     } else {
         // peel to a V-element boundary, full vectors, then the ragged tail
         int64_t pa = (p + V - 1) / V * V;
         if (pa > pe) pa = pe;
         for (int64_t q = p + lane; q < pa; q += TPR)
-            acc.mad(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg));
+            acc.mad(ld_stream(val + q, ps), gather_x<NA>(x + ld_stream(idx + q, ps), pg));
         const int64_t nv = (pe - pa) / V;
         int64_t k = lane;
         for (; k + (int64_t)(U - 1) * TPR < nv; k += (int64_t)TPR * U) {
@@ -79,7 +90,7 @@ __device__ __forceinline__ T row_dot(const I* __restrict__ idx, const T* __restr
 #pragma unroll
             for (int u = 0; u < U; ++u)
 #pragma unroll
-                for (int e = 0; e < V; ++e) acc.mad(v[u][e], ld_gather(x + c[u][e], pg));
+                for (int e = 0; e < V; ++e) acc.mad(v[u][e], gather_x<NA>(x + c[u][e], pg));
         }
         for (; k < nv; k += TPR) {
             int64_t c[V];
@@ -87,10 +98,10 @@ __device__ __forceinline__ T row_dot(const I* __restrict__ idx, const T* __restr
             const int64_t q = pa + k * V;
             ld_stream_vec<T, I, V>(idx + q, val + q, ps, c, v);
 #pragma unroll
-            for (int e = 0; e < V; ++e) acc.mad(v[e], ld_gather(x + c[e], pg));
+            for (int e = 0; e < V; ++e) acc.mad(v[e], gather_x<NA>(x + c[e], pg));
         }
         for (int64_t q = pa + nv * V + lane; q < pe; q += TPR)
-            acc.mad(ld_stream(val + q, ps), ld_gather(x + ld_stream(idx + q, ps), pg));
+            acc.mad(ld_stream(val + q, ps), gather_x<NA>(x + ld_stream(idx + q, ps), pg));
     }
     return acc.get();
 }
