@@ -2,11 +2,11 @@
 //
 // A CSR SpMV over uniformly scattered columns is bound by how fast the SMs can gather
 // 8-byte x values from random addresses (one 32-byte L2 sector per gather), not by the
-// HBM stream of indices and values.  This kernel performs the same gathers as the SpMV
-// -- the same column indices, the same load instruction and cache policy (ld.global.nc,
-// no L1 allocation, L2 evict_last), four gathers in flight per thread -- and nothing else (no values,
-// no row offsets, no row reductions, no output vector), so the time it takes is the
-// floor for the SpMV's gather traffic on this GPU.  Benchmarks report the SpMV's time
+// HBM stream of indices and values.  This kernel performs the same gathers as the power
+// step's SpMV -- the same column indices, the same load instruction and cache policy
+// (ld.global.nc, no L1 allocation, L2 evict_last), four gathers in flight per thread --
+// and nothing else (no values, no row offsets, no row reductions, no output vector), so
+// the time it takes is the floor for the SpMV's gather traffic on this GPU.  Benchmarks report the SpMV's time
 // against it next to the HBM roofline.
 //
 // A measurement aid only: it is built into its own library (libtg_gather_probe.so, loaded
