@@ -1048,6 +1048,11 @@ def main():
         kname = "spmv_stream_kernel(power)" if args.split == "stream" else (
             "power_p2p_kernel" if (world > 1 and args.exchange == "p2p") else "power_step_kernel")
         tr = traffic_record("c4_%d" % world, kname)
+        # 32-byte L2 sectors per launch: one per x gather (uniform random columns) plus the
+        # streamed arrays; the probe streams only the indices
+        ib = 4 if pi.index32 else 8
+        probe_sectors = shard.nnz + shard.nnz * ib / 32
+        step_sectors = shard.nnz + (shard.nnz * (ib + 8) + (r1 - r0 + 1) * 8 + (r1 - r0) * 8) / 32
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(achieved / peak, 4), "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"
                     if peak_kind == "measured" else "fallback 6.65 TB/s",
@@ -1059,9 +1064,16 @@ def main():
                         "gathers_per_s": round(shard.nnz / (gather_ms_local / 1e3), 1),
                         "step_ms": round(step_ms_local, 4),
                         "frac": round(gather_ms_local / step_ms_local, 4),
+                        "l2_sectors_probe": int(probe_sectors),
+                        "l2_sectors_step": int(step_sectors),
+                        "sector_rate_frac": round((step_sectors / step_ms_local) / (probe_sectors / gather_ms_local),
+                                                  4),
                         "what": "rank 0: tg_gather_probe_f64 on the shard's own column indices (the "
                                 "SpMV's x gathers alone, same load path and L2 policy) alternated with "
-                                "the plain power-step kernel; frac = probe time / step-kernel time"}}
+                                "the plain power-step kernel; frac = probe time / step-kernel time; "
+                                "sector_rate_frac = the step's 32-byte L2 sectors per second (one per "
+                                "gather plus its streamed indices, values, row offsets and output) over "
+                                "the probe's (one per gather plus its indices)"}}
         line = {
             "metric": "effective_hbm_gbs_power_iteration_spmv",
             "value": round(gbs, 2),
