@@ -617,6 +617,43 @@ def measure_matrix(wl: str, sched: dict, steps: int, warmup: int, rank: int, wor
                  "what": "event_floor_ms: the same flush then an event pair around a one-element op; "
                          "warm_ms: per call, 20 calls back to back in a CUDA graph, L2-resident"}
 
+    # C5: the dense-row gather floor -- the bench-only probe reads the same B (SpMM) or V
+    # (SDDMM) row for every nonzero and nothing else; alternated with the step so both see
+    # the same clocks
+    row_floor = None
+    if c5 and kernel in ("spmm", "sddmm"):
+        from tilegen_b200 import bench_probe
+
+        dense = d_in["B"] if kernel == "spmm" else d_in["V"]
+        pout = torch.zeros(1, dtype=torch.float64, device=dev)
+
+        def probe():
+            bench_probe.row_gather_probe_f32(Ad.indices.data_ptr(), S.nnz, dense.data_ptr(), int(dense.shape[1]),
+                                             pout.data_ptr(), stream.cuda_stream)
+
+        for _ in range(3):
+            probe()
+        pe, se = [], []
+        for _ in range(10):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record(stream)
+            probe()
+            ev[1].record(stream)
+            ev[2].record(stream)
+            step()
+            ev[3].record(stream)
+            pe.append((ev[0], ev[1]))
+            se.append((ev[2], ev[3]))
+        torch.cuda.synchronize(dev)
+        p_ms = float(np.median([a.elapsed_time(b) for a, b in pe]))
+        s_ms = float(np.median([a.elapsed_time(b) for a, b in se]))
+        row_bytes = int(dense.shape[1]) * dense.element_size()
+        row_floor = {"ms": round(p_ms, 5), "step_ms": round(s_ms, 5), "frac": round(p_ms / s_ms, 4),
+                     "gathered_gbs": round(S.nnz * row_bytes / (p_ms / 1e3) / 1e9, 1),
+                     "what": "tg_row_gather_probe_f32: the %d-byte %s row of every nonzero (same indices, load "
+                             "instruction and L2 policy) and nothing else, alternated with the step; frac = "
+                             "probe time / step time" % (row_bytes, "B" if kernel == "spmm" else "V")}
+
     # e2e through the public API: H2D of the step's dense inputs from pinned memory, the
     # call, D2H of the output shard
     e2e = []
@@ -637,7 +674,8 @@ def measure_matrix(wl: str, sched: dict, steps: int, warmup: int, rank: int, wor
            "e2e_local": float(np.mean(e2e)) if e2e else float("nan"), "launches": int(launches), "clocks": clocks,
            "wall": wall, "flush": flush is not None, "c5": c5, "inputs": inputs, "schedule": dict(sched),
            "h2d": int(sum(v.numel() * v.element_size() for v in h_in.values())),
-           "d2h": int(h_out.numel() * h_out.element_size()), "plan": plan, "floor": floor, "reorder": reorder}
+           "d2h": int(h_out.numel() * h_out.element_size()), "plan": plan, "floor": floor, "reorder": reorder,
+           "row_floor": row_floor}
     if want_cusparse:
         rec["cusparse"] = cusparse_compare(wl, Ad, d_in, flush, steps, matrix_bytes(wl, A))
     if want_cpu:
@@ -704,6 +742,8 @@ def summarise_matrix(rec, ms_step: float, world: int, peak: float):
         d["timing_floor"] = rec["floor"]
     if rec.get("reorder"):
         d["reorder"] = rec["reorder"]
+    if rec.get("row_floor"):
+        d["row_gather_floor"] = rec["row_floor"]
     if "cusparse" in rec:
         c = rec["cusparse"]
         d["cusparse"] = c
@@ -785,6 +825,8 @@ def run_matrix_workload(args, rank: int, world: int, local_rank: int):
             line["timing_floor"] = rec["floor"]
         if rec.get("reorder"):
             line["reorder"] = rec["reorder"]
+        if rec.get("row_floor"):
+            line["roofline"]["row_gather_floor"] = rec["row_floor"]
         if "cusparse" in rec:
             line["cusparse"] = rec["cusparse"]
         if "cpu_baseline" in rec:

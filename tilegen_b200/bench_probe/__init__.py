@@ -1,5 +1,6 @@
-"""The benchmark's gather-floor probe (libtg_gather_probe.so): the random x gathers of a
-CSR SpMV and nothing else.  A measurement aid, kept out of libtilegen_b200.so."""
+"""The benchmark's gather-floor probes (libtg_gather_probe.so): the random x gathers of a
+CSR SpMV, or the dense-row gathers of an SpMM / SDDMM, and nothing else.  A measurement
+aid, kept out of libtilegen_b200.so."""
 
 from __future__ import annotations
 
@@ -23,6 +24,9 @@ def load() -> ctypes.CDLL:
             fn = getattr(L, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        L.tg_row_gather_probe_f32.restype = ctypes.c_int
+        L.tg_row_gather_probe_f32.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                                              ctypes.c_void_p, ctypes.c_void_p]
         _probe = L
     return _probe
 
@@ -35,3 +39,11 @@ def gather_probe_f64(indices_ptr: int, n: int, x_ptr: int, out_ptr: int, stream:
     rc = fn(indices_ptr, n, x_ptr, out_ptr, stream)
     if rc != 0:
         raise RuntimeError("tg_gather_probe_f64 failed with status %d" % rc)
+
+
+def row_gather_probe_f32(indices_ptr: int, n: int, B_ptr: int, K: int, out_ptr: int, stream: int) -> None:
+    """*out += sum of B[indices[i], :] for i < n, on `stream` (device pointers; int64
+    indices; B row-major fp32 with K = 64 or 128 columns, 16-byte aligned)."""
+    rc = load().tg_row_gather_probe_f32(indices_ptr, n, B_ptr, K, out_ptr, stream)
+    if rc != 0:
+        raise RuntimeError("tg_row_gather_probe_f32 failed with status %d" % rc)
