@@ -143,14 +143,23 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.first = ""
 
     def start(self):
+        """Start sampling and wait (up to 5 s) for the first sample, so that a timed region
+        shorter than the sampling period still has the sample taken as it begins."""
+        import select
+
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.FIELDS,
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        ready, _, _ = select.select([self.proc.stdout], [], [], 5.0)
+        if ready:
+            self.first = self.proc.stdout.readline()
 
     def stop(self):
         if self.proc is None:
@@ -161,6 +170,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
+        out = self.first + out
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.splitlines():
